@@ -1,0 +1,586 @@
+// Chunkwise GDN2 forward (C = 64): the reference pipeline
+//   chunk_gdn2_fwd (lit_gpt/gdn2_ops/chunk_gdn2.py:1205-1359)
+//   = gate cumsum -> intra scores -> (I+T)^-1 -> WY factors -> state scan + o
+// as two B200 kernels:
+//
+// chunk_intra_kernel (one CTA per (chunk, head), chunk-parallel):
+//   - optional l2norm of q, k (fla l2norm_fwd, eps 1e-6 inside the sqrt),
+//     rounded to bf16 as the reference's l2norm output is;
+//   - optional gate activation, then G = chunk-local cumsum(g) / ln 2;
+//   - Aqk = scale (q 2^G)(k 2^-G)^T (lower incl. diagonal) and
+//     T = (b k 2^G)(k 2^-G)^T (strictly lower) on tensor cores, with every
+//     exponent anchored at the first row a of the 16-row block it belongs to:
+//         2^(G_r - G_s) = 2^(G_r - G_a) * 2^(G_a - G_s).
+//     For s < a both factors are <= 1 (exact for any gates).  Inside the
+//     diagonal 16x16 block the column factor grows with the block's decay
+//     range; a (block, channel) whose range exceeds 2^96 is dropped from the
+//     tensor-core operand and its exact contribution is added pair by pair
+//     (exp2 per pair), so the scores are exact for arbitrary gates.  (The
+//     reference instead clamps mid-anchored exponents at 2^110,
+//     chunk_gdn2.py:457-471, and is exact only below that.)
+//   - A = (I+T)^-1 in fp32 on CUDA cores: 16x16 diagonal blocks by forward
+//     substitution, off-diagonal blocks A_ij = -A_ii sum_m T_im A_mj;
+//   - Y = A (b k 2^G), U = A (w v) on tensor cores; kg = k 2^(G_last - G),
+//     qg = q 2^G (recompute_w_u_fwd_gdn2_kernel, chunk_gdn2.py:837-929).
+//
+// chunk_scan_fwd_kernel (one CTA per (sequence, head, 64-column V tile)):
+//   serial over the chunks of the sequence with the [K x 64] fp32 state in
+//   tensor-core accumulator registers (chunk_gated_delta_rule_fwd_h,
+//   chunk_kda.py:983-1335, with its fused output):
+//     v_new = U - Y S ; o = scale qg S + Aqk v_new ; S <- 2^G_last * S + kg^T v_new
+//   The next chunk's operands are prefetched with cp.async while the current
+//   chunk computes.
+#include "common.cuh"
+#include "chunk_layout.cuh"
+
+namespace gdn2 {
+
+// ---------------------------------------------------------------------------
+// F1: chunk-parallel intra kernel
+// ---------------------------------------------------------------------------
+constexpr float kAnchorRange = 96.f;  // max log2 decay range kept on the tensor-core path
+constexpr int kIntraThreads = 256;
+
+template <int K, int V>
+struct IntraSmem {
+  static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 4, LAB = kChunk + 8;
+  float G[kChunk][K];
+  __nv_bfloat16 Q[kChunk][LK];
+  __nv_bfloat16 Kt[kChunk][LK];
+  float Aqk[kChunk][LA];
+  float Tm[kChunk][LA];
+  float Af[kChunk][LA];
+  __nv_bfloat16 Ab[kChunk][LAB];
+  union {
+    struct {
+      __nv_bfloat16 QG[kChunk][LK];
+      __nv_bfloat16 KBG[kChunk][LK];
+      __nv_bfloat16 KN[160][LK];  // anchors 0..3: rows [0,16), [16,48), [48,96), [96,160)
+    } s;
+    struct {
+      __nv_bfloat16 KB2G[kChunk][LK];
+      __nv_bfloat16 WV[kChunk][LV];
+    } w;
+  } u;
+  float P[4][16][17];        // solve scratch
+  float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
+  uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
+  int nflag[4];
+};
+
+template <typename TB>
+GDN2_DEV float ld_bw(const void* p, int64_t i) {
+  return to_f(static_cast<const TB*>(p)[i]);
+}
+
+template <int K, int V, typename TB>
+__global__ void __launch_bounds__(kIntraThreads, 1)
+chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = IntraSmem<K, V>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t H = a.H;
+  const int64_t h = blockIdx.y;
+  const int64_t cglob = blockIdx.x;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t n, ci, bos, len;
+  geo.chunk(cglob, n, ci);
+  geo.seq(n, bos, len);
+  const int64_t t0 = bos + ci * kChunk;  // first token of the chunk
+  const int L = (int)(kChunk < (len - ci * kChunk) ? (int64_t)kChunk : (len - ci * kChunk));
+  const bool l2 = a.flags & GDN2_L2NORM_QK;
+  const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  const __nv_bfloat16* qin = static_cast<const __nv_bfloat16*>(a.q);
+  const __nv_bfloat16* kin = static_cast<const __nv_bfloat16*>(a.k);
+  const __nv_bfloat16* vin = static_cast<const __nv_bfloat16*>(a.v);
+
+  // ---- 1. q, k rows (+ l2norm) ---------------------------------------------
+  // warp w owns rows 8w..8w+7; lane owns channels lane, lane+32, ...
+  for (int rr = 0; rr < 8; ++rr) {
+    const int r = warp * 8 + rr;
+    float qv[K / 32], kv[K / 32];
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int j = 0; j < K / 32; ++j) {
+      const int c = lane + 32 * j;
+      if (r < L) {
+        const int64_t idx = ((t0 + r) * H + h) * K + c;
+        qv[j] = to_f(qin[idx]);
+        kv[j] = to_f(kin[idx]);
+      } else {
+        qv[j] = 0.f;
+        kv[j] = 0.f;
+      }
+      sq += qv[j] * qv[j];
+      sk += kv[j] * kv[j];
+    }
+    float rq = 1.f, rk = 1.f;
+    if (l2) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        sk += __shfl_xor_sync(0xffffffffu, sk, off);
+      }
+      rq = rsqrtf(sq + kL2Eps);
+      rk = rsqrtf(sk + kL2Eps);
+      if (save && r < L && lane == 0) {
+        ws.q_rstd[(t0 + r) * H + h] = rq;
+        ws.k_rstd[(t0 + r) * H + h] = rk;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < K / 32; ++j) {
+      const int c = lane + 32 * j;
+      const __nv_bfloat16 qb = __float2bfloat16_rn(qv[j] * rq);
+      const __nv_bfloat16 kb = __float2bfloat16_rn(kv[j] * rk);
+      sm.Q[r][c] = qb;
+      sm.Kt[r][c] = kb;
+      if (l2 && save && r < L) {
+        const int64_t idx = ((t0 + r) * H + h) * K + c;
+        ws.qn[idx] = qb;
+        ws.kn[idx] = kb;
+      }
+    }
+  }
+
+  // ---- 2. gate activation + chunk-local cumsum (log2 units) ----------------
+  const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
+  const bool lbnd = a.flags & GDN2_LOWER_BOUND;
+  for (int c = tid; c < K; c += kIntraThreads) {
+    const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
+    const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
+    float Gc = 0.f;
+    for (int r0 = 0; r0 < kChunk; r0 += 8) {
+      float gv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + j;
+        gv[j] = r < L ? a.g[((t0 + r) * H + h) * K + c] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = r0 + j;
+        float x = gv[j];
+        if (gate) {
+          x += bias;
+          x = lbnd ? a.lower_bound * sigmoid_f(Aexp * x) : -Aexp * softplus_f(x);
+        }
+        if (r < L) Gc += x * kRcpLn2;
+        sm.G[r][c] = Gc;  // padded rows repeat G_last
+        if (r < L) ws.G[((t0 + r) * H + h) * K + c] = Gc;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 3. anchored tensor-core operands ------------------------------------
+  for (int i = tid; i < 4 * K; i += kIntraThreads) {
+    const int blk = i / K, c = i % K;
+    const int a0 = blk * 16;
+    const int alast = min(a0 + 15, max(L - 1, 0));
+    const float range = sm.G[a0][c] - sm.G[alast][c];
+    sm.flag[blk][c] = range > kAnchorRange ? 1 : 0;
+    sm.Dblk[blk][c] = blk > 0 ? exp2_approx(sm.G[a0][c] - sm.G[a0 - 16][c]) : 1.f;
+  }
+  if (tid < 4) sm.nflag[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < 4 * K; i += kIntraThreads) {
+    if (sm.flag[i / K][i % K]) atomicAdd(&sm.nflag[i / K], 1);
+  }
+  for (int i = tid; i < kChunk * K; i += kIntraThreads) {
+    const int r = i / K, c = i % K;
+    const int blk = r >> 4, a0 = blk * 16;
+    const float kq = __bfloat162float(sm.Kt[r][c]);
+    const float qq = __bfloat162float(sm.Q[r][c]);
+    const float bb = r < L ? ((a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.b, ((t0 + r) * H + h) * K + c)
+                                                      : ld_bw<float>(a.b, ((t0 + r) * H + h) * K + c))
+                           : 0.f;
+    const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);  // <= 1
+    sm.u.s.QG[r][c] = __float2bfloat16_rn(qq * rowf);
+    sm.u.s.KBG[r][c] = __float2bfloat16_rn(bb * kq * rowf);
+    // column operands for every anchor at or after this row's block
+    const bool fl = sm.flag[blk][c];
+    const float fd = fl ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);  // >= 1, bounded
+    sm.u.s.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kq * fd);
+    if (blk < 3) {
+      float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);  // <= 1
+      for (int ai = blk + 1; ai < 4; ++ai) {
+        if (ai > blk + 1) f *= sm.Dblk[ai][c];
+        sm.u.s.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kq * f);
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 4. scores on tensor cores -------------------------------------------
+  // tiles (i, j <= i) for Aqk and T: 20 tiles of 16x16 over 8 warps
+  for (int tile = warp; tile < 20; tile += 8) {
+    const int mat = tile & 1;  // 0: Aqk, 1: T
+    int tt = tile >> 1, bi = 0;
+    while (tt > bi) {
+      tt -= bi + 1;
+      ++bi;
+    }
+    const int bj = tt;
+    float acc[1][2][4];
+    zero_acc(acc);
+    Smem Aop{mat == 0 ? &sm.u.s.QG[0][0] : &sm.u.s.KBG[0][0], S::LK};
+    Smem Bop{&sm.u.s.KN[anchor_row0(bi)][0], S::LK};
+    warp_mma<1, 2, false, true>(acc, Aop, bi * 16, Bop, bj * 16, 0, K, lane);
+    const float sc = mat == 0 ? a.scale : 1.f;
+    acc_foreach(acc, bi * 16, bj * 16, lane, [&](float v, int r, int s) {
+      const bool keep = (mat == 0 ? s <= r : s < r) && r < L;
+      if (mat == 0) sm.Aqk[r][s] = keep ? v * sc : 0.f;
+      else sm.Tm[r][s] = keep ? v : 0.f;
+    });
+  }
+  // upper-triangle blocks are zero
+  for (int i = tid; i < 6 * 256; i += kIntraThreads) {
+    const int blkp = i / 256, e = i % 256;
+    static const int ui[6] = {0, 0, 0, 1, 1, 2}, uj[6] = {1, 2, 3, 2, 3, 3};
+    const int r = ui[blkp] * 16 + e / 16, s = uj[blkp] * 16 + e % 16;
+    sm.Aqk[r][s] = 0.f;
+    sm.Tm[r][s] = 0.f;
+  }
+  __syncthreads();
+
+  // ---- 5. exact pairs for (block, channel)s beyond the anchored range ------
+  for (int blk = 0; blk < 4; ++blk) {
+    if (sm.nflag[blk] == 0) continue;
+    if (tid < 136) {
+      int rr = 0, p = tid;  // pair index -> (r >= s) inside the 16x16 block
+      while (p > rr) {
+        p -= rr + 1;
+        ++rr;
+      }
+      const int r = blk * 16 + rr, s = blk * 16 + p;
+      if (r < L) {
+        float aq = 0.f, at = 0.f;
+        for (int c = 0; c < K; ++c) {
+          if (!sm.flag[blk][c]) continue;
+          const float e = exp2f(sm.G[r][c] - sm.G[s][c]);
+          const float ks = __bfloat162float(sm.Kt[s][c]);
+          const float kr = __bfloat162float(sm.Kt[r][c]);
+          const float bb = (a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.b, ((t0 + r) * H + h) * K + c)
+                                                     : ld_bw<float>(a.b, ((t0 + r) * H + h) * K + c);
+          aq += __bfloat162float(sm.Q[r][c]) * ks * e;
+          at += bb * kr * ks * e;
+        }
+        sm.Aqk[r][s] += a.scale * aq;
+        if (s < r) sm.Tm[r][s] += at;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 6. A = (I + T)^-1 (fp32) --------------------------------------------
+  // 6a: diagonal 16x16 blocks by forward substitution; warp b < 4 owns block b,
+  //     lane j < 16 owns column j.
+  if (warp < 4 && lane < 16) {
+    const int o = warp * 16, j = lane;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float acc = (r == j) ? 1.f : 0.f;
+#pragma unroll
+      for (int s = 0; s < r; ++s) acc -= sm.Tm[o + r][o + s] * x[s];
+      x[r] = acc;
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sm.Af[o + r][o + j] = x[r];
+  }
+  __syncthreads();
+  // 6b: off-diagonal blocks by increasing distance d = i - j
+  for (int d = 1; d < 4; ++d) {
+    const int nb = 4 - d;
+    // P_j = sum_{m=j}^{i-1} T_im A_mj for each block (j+d, j)
+    for (int e = tid; e < nb * 256; e += kIntraThreads) {
+      const int jb = e / 256, rc = e % 256, r = rc / 16, c = rc % 16;
+      const int ib = jb + d;
+      float acc = 0.f;
+      for (int m = jb; m < ib; ++m)
+#pragma unroll
+        for (int x = 0; x < 16; ++x) acc += sm.Tm[ib * 16 + r][m * 16 + x] * sm.Af[m * 16 + x][jb * 16 + c];
+      sm.P[jb][r][c] = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 256; e += kIntraThreads) {
+      const int jb = e / 256, rc = e % 256, r = rc / 16, c = rc % 16;
+      const int ib = jb + d;
+      float acc = 0.f;
+#pragma unroll
+      for (int x = 0; x < 16; ++x) acc += sm.Af[ib * 16 + r][ib * 16 + x] * sm.P[jb][x][c];
+      sm.Af[ib * 16 + r][jb * 16 + c] = -acc;
+    }
+    __syncthreads();
+  }
+  // upper blocks of A are zero; bf16 copy; Aqk / A to global
+  for (int i = tid; i < kChunk * kChunk; i += kIntraThreads) {
+    const int r = i / kChunk, s = i % kChunk;
+    const float av = s > r ? 0.f : ((r < L || s == r) ? sm.Af[r][s] : 0.f);
+    const __nv_bfloat16 ab = __float2bfloat16_rn(av);
+    sm.Ab[r][s] = ab;
+    if (r < L) {
+      const int64_t gi = ((t0 + r) * H + h) * kChunk + s;
+      ws.Akk[gi] = ab;
+      ws.Aqk[gi] = __float2bfloat16_rn(sm.Aqk[r][s]);
+    }
+  }
+  // WY operands (the score operands are dead now)
+  __syncthreads();
+  for (int i = tid; i < kChunk * K; i += kIntraThreads) {
+    const int r = i / K, c = i % K;
+    const float bb = r < L ? ((a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.b, ((t0 + r) * H + h) * K + c)
+                                                      : ld_bw<float>(a.b, ((t0 + r) * H + h) * K + c))
+                           : 0.f;
+    const float kq = __bfloat162float(sm.Kt[r][c]);
+    const float qq = __bfloat162float(sm.Q[r][c]);
+    const float Gr = sm.G[r][c];
+    const float e = exp2_approx(Gr);
+    sm.u.w.KB2G[r][c] = __float2bfloat16_rn(bb * kq * e);
+    if (r < L) {
+      const int64_t gi = ((t0 + r) * H + h) * K + c;
+      ws.kg[gi] = __float2bfloat16_rn(kq * exp2_approx(sm.G[kChunk - 1][c] - Gr));
+      ws.qg[gi] = __float2bfloat16_rn(qq * e);
+    }
+  }
+  for (int i = tid; i < kChunk * V; i += kIntraThreads) {
+    const int r = i / V, c = i % V;
+    float wv = 0.f;
+    if (r < L) {
+      const int64_t gi = ((t0 + r) * H + h) * V + c;
+      const float ww = (a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.w, gi) : ld_bw<float>(a.w, gi);
+      wv = ww * __bfloat162float(vin[gi]);
+    }
+    sm.u.w.WV[r][c] = __float2bfloat16_rn(wv);
+  }
+  __syncthreads();
+
+  // ---- 7. Y = A (b k 2^G), U = A (w v) ---------------------------------------
+  // each warp: 16 rows x (K/2) cols of Y, then of U
+  {
+    const int m0 = (warp & 3) * 16;
+    Smem Aop{&sm.Ab[0][0], S::LAB};
+    {
+      constexpr int NTc = K / 2 / 8;
+      const int n0 = (warp >> 2) * (K / 2);
+      float acc[1][NTc][4];
+      zero_acc(acc);
+      warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.u.w.KB2G[0][0], S::LK}, n0, 0, kChunk, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
+        if (r < L) ws.Y[((t0 + r) * H + h) * K + c] = __float2bfloat16_rn(v);
+      });
+    }
+    {
+      constexpr int NTc = V / 2 / 8;
+      const int n0 = (warp >> 2) * (V / 2);
+      float acc[1][NTc][4];
+      zero_acc(acc);
+      warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.u.w.WV[0][0], S::LV}, n0, 0, kChunk, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
+        if (r < L) ws.U[((t0 + r) * H + h) * V + c] = __float2bfloat16_rn(v);
+      });
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// F2: inter-chunk state scan with the fused output
+// ---------------------------------------------------------------------------
+constexpr int kScanThreads = 256;
+constexpr int kScanBV = 64;
+
+template <int K>
+struct ScanStage {
+  static constexpr int LK = K + 8, LV = kScanBV + 8, LA = kChunk + 8;
+  __nv_bfloat16 Y[kChunk][LK];
+  __nv_bfloat16 QG[kChunk][LK];
+  __nv_bfloat16 KG[kChunk][LK];
+  __nv_bfloat16 Aqk[kChunk][LA];
+  __nv_bfloat16 U[kChunk][LV];
+  float glast[K];
+};
+
+template <int K>
+struct ScanSmem {
+  ScanStage<K> st[2];
+  __nv_bfloat16 Sb[K][kScanBV + 8];      // bf16 copy of the state (MMA operand)
+  __nv_bfloat16 VN[kChunk][kScanBV + 8]; // v_new (bf16)
+};
+
+GDN2_DEV void cp_async16(void* dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(n));
+}
+GDN2_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+GDN2_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+template <int K, int V>
+GDN2_DEV void scan_prefetch(ScanStage<K>& st, const ChunkWs& ws, const gdn2_chunk_args& a, int64_t t0, int L,
+                            int64_t h, int v0, int tid) {
+  const int64_t H = a.H;
+  // rows of K bf16 = K/8 16-byte pieces
+  for (int i = tid; i < kChunk * (K / 8); i += kScanThreads) {
+    const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+    const bool ok = r < L;
+    const int64_t gi = ((t0 + (ok ? r : 0)) * H + h) * K + p;
+    cp_async16(&st.Y[r][p], ws.Y + gi, ok);
+    cp_async16(&st.QG[r][p], ws.qg + gi, ok);
+    cp_async16(&st.KG[r][p], ws.kg + gi, ok);
+  }
+  for (int i = tid; i < kChunk * (kChunk / 8); i += kScanThreads) {
+    const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
+    const bool ok = r < L;
+    cp_async16(&st.Aqk[r][p], ws.Aqk + ((t0 + (ok ? r : 0)) * H + h) * kChunk + p, ok);
+  }
+  for (int i = tid; i < kChunk * (kScanBV / 8); i += kScanThreads) {
+    const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
+    const bool ok = r < L;
+    cp_async16(&st.U[r][p], ws.U + ((t0 + (ok ? r : 0)) * H + h) * V + v0 + p, ok);
+  }
+  for (int i = tid; i < K / 4; i += kScanThreads)
+    cp_async16(&st.glast[i * 4], ws.G + ((t0 + L - 1) * H + h) * K + i * 4, true);
+}
+
+template <int K, int V>
+__global__ void __launch_bounds__(kScanThreads, 1)
+chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  ScanSmem<K>& sm = *reinterpret_cast<ScanSmem<K>*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t H = a.H;
+  const int v0 = blockIdx.x * kScanBV;
+  const int64_t n = blockIdx.y / H, h = blockIdx.y % H;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t bos, len;
+  geo.seq(n, bos, len);
+  const int64_t nchunks = (len + kChunk - 1) / kChunk;
+  const int64_t c0 = geo.chunk0(n);
+  const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
+  const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.o);
+
+  // state accumulators: warp w owns rows [16w, 16w+16) (K=128: 8 warps) x 64 cols
+  constexpr int kRowsPerWarp = K / 8;  // 16 (K=128) or 8 (K=64)
+  constexpr int MT = kRowsPerWarp >= 16 ? kRowsPerWarp / 16 : 1;
+  constexpr int NT = kScanBV / 8;
+  float S[MT][NT][4];
+  const int sm0 = warp * kRowsPerWarp;
+  const bool srows = kRowsPerWarp >= 16;  // K=64: only warps 0..3 hold state rows
+  const bool sown = srows || warp < 4;
+  const int sr0 = srows ? sm0 : warp * 16;
+  acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
+    float x = 0.f;
+    if (sown && (a.flags & GDN2_HAS_H0)) {
+      const float* h0 = a.h0 + (n * H + h) * (int64_t)K * V;
+      x = tr ? h0[(int64_t)(v0 + c) * K + r] : h0[(int64_t)r * V + v0 + c];
+    }
+    v = x;
+  });
+
+  if (nchunks > 0) {
+    const int L0 = (int)(kChunk < (len) ? (int64_t)kChunk : (len));
+    scan_prefetch<K, V>(sm.st[0], ws, a, bos, L0, h, v0, tid);
+  }
+  cp_async_commit();
+
+  for (int64_t ci = 0; ci < nchunks; ++ci) {
+    const int64_t t0 = bos + ci * kChunk;
+    const int L = (int)(kChunk < (len - ci * kChunk) ? (int64_t)kChunk : (len - ci * kChunk));
+    ScanStage<K>& st = sm.st[ci & 1];
+    // state -> bf16 operand (and the saved per-chunk state h)
+    if (sown) {
+      acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(v);
+        sm.Sb[r][c] = b;
+        if (save) {
+          __nv_bfloat16* hdst = ws.h + ((c0 + ci) * H + h) * (int64_t)K * V;
+          hdst[(int64_t)r * V + v0 + c] = b;
+        }
+      });
+    }
+    if (ci + 1 < nchunks) {
+      const int Ln = (int)(kChunk < (len - (ci + 1) * kChunk) ? (int64_t)kChunk : (len - (ci + 1) * kChunk));
+      scan_prefetch<K, V>(sm.st[(ci + 1) & 1], ws, a, t0 + kChunk, Ln, h, v0, tid);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+
+    // v_new = U - Y S : warp tile 16 rows x 32 cols (8 warps cover 64 x 64)
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+    {
+      float acc[1][4][4];
+      zero_acc(acc);
+      warp_mma<1, 4, false, false>(acc, Smem{&st.Y[0][0], ScanStage<K>::LK}, m0, Smem{&sm.Sb[0][0], kScanBV + 8},
+                                   n0, 0, K, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
+        const float vn = r < L ? __bfloat162float(st.U[r][c]) - v : 0.f;
+        const __nv_bfloat16 b = __float2bfloat16_rn(vn);
+        sm.VN[r][c] = b;
+        if (save && r < L) ws.v_new[((t0 + r) * H + h) * V + v0 + c] = b;
+      });
+    }
+    __syncthreads();
+    // o = scale * qg S + Aqk v_new
+    {
+      float acc[1][4][4];
+      zero_acc(acc);
+      warp_mma<1, 4, false, false>(acc, Smem{&st.QG[0][0], ScanStage<K>::LK}, m0, Smem{&sm.Sb[0][0], kScanBV + 8},
+                                   n0, 0, K, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float& v, int, int) { v *= a.scale; });
+      warp_mma<1, 4, false, false>(acc, Smem{&st.Aqk[0][0], ScanStage<K>::LA}, m0,
+                                   Smem{&sm.VN[0][0], kScanBV + 8}, n0, 0, kChunk, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
+        if (r < L) o[((t0 + r) * H + h) * V + v0 + c] = __float2bfloat16_rn(v);
+      });
+    }
+    // S <- 2^G_last S + kg^T v_new
+    if (sown) {
+      acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int) { v *= exp2_approx(st.glast[r]); });
+      warp_mma<MT, NT, true, false>(S, Smem{&st.KG[0][0], ScanStage<K>::LK}, sr0, Smem{&sm.VN[0][0], kScanBV + 8},
+                                    0, 0, kChunk, lane);
+    }
+    __syncthreads();  // stage buffers and Sb are rewritten next iteration
+  }
+  cp_async_wait<0>();
+
+  if (sown && (a.flags & GDN2_STORE_FINAL)) {
+    float* ht = a.ht + (n * H + h) * (int64_t)K * V;
+    acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
+      if (tr) ht[(int64_t)(v0 + c) * K + r] = v;
+      else ht[(int64_t)r * V + v0 + c] = v;
+    });
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int K, int V>
+int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
+  if (a.NT > 0) {
+    const size_t sm1 = sizeof(IntraSmem<K, V>);
+    auto k1 = a.dtype_bw == GDN2_BF16 ? chunk_intra_kernel<K, V, __nv_bfloat16> : chunk_intra_kernel<K, V, float>;
+    GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
+    dim3 g1((unsigned)a.NT, (unsigned)a.H);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
+    GDN2_LAUNCH_CHECK();
+  }
+  const size_t sm2 = sizeof(ScanSmem<K>);
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sm2));
+  dim3 g2((unsigned)(V / kScanBV), (unsigned)(a.N * a.H));
+  chunk_scan_fwd_kernel<K, V><<<g2, kScanThreads, sm2, s>>>(a, ws);
+  GDN2_LAUNCH_CHECK();
+  return 0;
+}
+
+int chunk_fwd_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
+  if (a.K == 128 && a.V == 128) return launch_fwd_kv<128, 128>(a, ws, s);
+  if (a.K == 128 && a.V == 64) return launch_fwd_kv<128, 64>(a, ws, s);
+  if (a.K == 64 && a.V == 128) return launch_fwd_kv<64, 128>(a, ws, s);
+  return launch_fwd_kv<64, 64>(a, ws, s);
+}
+
+}  // namespace gdn2

@@ -1,0 +1,94 @@
+// Layout of the chunk workspace: the forward's scratch (WY factors the scan
+// consumes) plus what the backward reads back.  Host and device share it.
+#pragma once
+#include "common.cuh"
+
+namespace gdn2 {
+
+struct ChunkWs {
+  // token-major [tokens, H, *] like the inputs
+  __nv_bfloat16* qn;   // normalised q (l2norm) — aliases q otherwise
+  __nv_bfloat16* kn;
+  float* q_rstd;       // [tokens, H]
+  float* k_rstd;
+  float* G;            // chunk-local cumsum of the (activated) gate, log2 units
+  __nv_bfloat16* Aqk;  // [tokens, H, 64]
+  __nv_bfloat16* Akk;  // (I+T)^-1, [tokens, H, 64]
+  __nv_bfloat16* Y;    // A (b k 2^G)           [tokens, H, K]
+  __nv_bfloat16* U;    // A (w v)               [tokens, H, V]
+  __nv_bfloat16* kg;   // k 2^(G_last - G)      [tokens, H, K]
+  __nv_bfloat16* qg;   // q 2^G                 [tokens, H, K]
+  __nv_bfloat16* v_new;// [tokens, H, V]
+  __nv_bfloat16* h;    // per-chunk entering state [NT, H, K, V]
+};
+
+struct BwdWs {
+  __nv_bfloat16* dh;   // state cotangent at the end of each chunk [NT, H, K, V]
+  __nv_bfloat16* dvn;  // cotangent of v_new [tokens, H, V]
+};
+
+inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Carves `base` (or computes the size when base == nullptr).
+inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws) {
+  const size_t tok = (size_t)a.B * (size_t)a.T;
+  const size_t H = (size_t)a.H, K = (size_t)a.K, V = (size_t)a.V;
+  const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  const bool l2 = a.flags & GDN2_L2NORM_QK;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes);
+    return base ? (void*)((char*)base + o) : nullptr;
+  };
+  ChunkWs w{};
+  w.G = (float*)take(tok * H * K * 4);
+  w.Aqk = (__nv_bfloat16*)take(tok * H * 64 * 2);
+  w.Akk = (__nv_bfloat16*)take(tok * H * 64 * 2);
+  w.Y = (__nv_bfloat16*)take(tok * H * K * 2);
+  w.U = (__nv_bfloat16*)take(tok * H * V * 2);
+  w.kg = (__nv_bfloat16*)take(tok * H * K * 2);
+  w.qg = (__nv_bfloat16*)take(tok * H * K * 2);
+  if (save) {
+    w.v_new = (__nv_bfloat16*)take(tok * H * V * 2);
+    w.h = (__nv_bfloat16*)take((size_t)a.NT * H * K * V * 2);
+    if (l2) {
+      w.qn = (__nv_bfloat16*)take(tok * H * K * 2);
+      w.kn = (__nv_bfloat16*)take(tok * H * K * 2);
+      w.q_rstd = (float*)take(tok * H * 4);
+      w.k_rstd = (float*)take(tok * H * 4);
+    }
+  }
+  if (!l2) {
+    w.qn = (__nv_bfloat16*)a.q;
+    w.kn = (__nv_bfloat16*)a.k;
+  }
+  if (ws) *ws = w;
+  return off;
+}
+
+inline size_t bwd_ws_layout(const gdn2_chunk_args& a, void* base, BwdWs* ws) {
+  const size_t tok = (size_t)a.B * (size_t)a.T;
+  const size_t H = (size_t)a.H, K = (size_t)a.K, V = (size_t)a.V;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes);
+    return base ? (void*)((char*)base + o) : nullptr;
+  };
+  BwdWs w{};
+  w.dh = (__nv_bfloat16*)take((size_t)a.NT * H * K * V * 2);
+  w.dvn = (__nv_bfloat16*)take(tok * H * V * 2);
+  if (ws) *ws = w;
+  return off;
+}
+
+// first row of anchor i's section in the KN operand: 0, 16, 48, 96
+GDN2_DEV constexpr int anchor_row0(int i) { return 8 * i * (i + 1); }
+
+int chunk_fwd_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
+int chunk_bwd_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                     cudaStream_t s);
+int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s);
+
+}  // namespace gdn2

@@ -1,0 +1,206 @@
+/*
+ * gdn2.h — C ABI of the B200 (sm_100a) Gated Delta Rule-2 operator.
+ *
+ * The operator keeps a per-(sequence, head) matrix state S in R^{K x V} (fp32)
+ * and, per token, applies
+ *
+ *     S <- Diag(exp(g_t)) S
+ *     u  = w_t * v_t - S^T (b_t * k_t)
+ *     S <- S + k_t u^T
+ *     o_t = S^T (scale * q_t)
+ *
+ * Three entry points carry the hot path:
+ *   gdn2_chunk_fwd      chunkwise (C = 64) forward used for training/prefill;
+ *   gdn2_chunk_bwd      its backward (dq, dk, dv, dg, db, dw, dh0, dA_log, ddt_bias);
+ *   gdn2_recurrent_fwd  the token-serial decode step.
+ * A context-parallel long-sequence mode adds
+ *   gdn2_cp_transition  a shard's boundary affine map (M, h_e);
+ *   gdn2_cp_compose     the exclusive prefix of those maps over ranks.
+ *
+ * Conventions shared by every entry point
+ *   - Pointers are device pointers unless stated otherwise.  Tensors are dense
+ *     and row-major in the reference's layouts: q, k, g, b are [B, T, H, K];
+ *     v, w, o are [B, T, H, V]; states are [N, H, K, V] (or [N, H, V, K] with
+ *     GDN2_TRANSPOSE_STATE).  With cu_seqlens (packed varlen) B must be 1 and
+ *     the N sequences are the spans [cu[i], cu[i+1]) of the T axis.
+ *   - The caller allocates every buffer, including the workspaces whose sizes
+ *     the *_workspace_size queries return.  No entry point allocates memory.
+ *   - Work is enqueued on `stream`; nothing synchronises the host.
+ *   - Return value: 0 on success, > 0 for an invalid argument (nothing was
+ *     launched), < 0 for a CUDA error (-(cudaError_t)).  gdn2_status_string()
+ *     names the code.
+ */
+#ifndef GDN2_B200_H_
+#define GDN2_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gdn2_stream_t; /* == cudaStream_t */
+
+/* element types */
+enum gdn2_dtype { GDN2_BF16 = 0, GDN2_F32 = 1 };
+
+/* option flags */
+enum gdn2_flags {
+  GDN2_L2NORM_QK = 1 << 0,       /* use_qk_l2norm_in_kernel (eps 1e-6 inside the sqrt) */
+  GDN2_GATE_IN_KERNEL = 1 << 1,  /* g is raw: g <- -exp(A_log) * softplus(g + dt_bias) */
+  GDN2_LOWER_BOUND = 1 << 2,     /* with GATE_IN_KERNEL: g <- lower_bound * sigmoid(exp(A_log)*(g+dt_bias)) */
+  GDN2_TRANSPOSE_STATE = 1 << 3, /* states stored [.., V, K] */
+  GDN2_HAS_H0 = 1 << 4,          /* initial_state given */
+  GDN2_STORE_FINAL = 1 << 5,     /* write the final state to `ht` */
+  GDN2_SAVE_FOR_BWD = 1 << 6     /* chunk fwd: keep what gdn2_chunk_bwd needs in the workspace */
+};
+
+/* status codes (> 0: invalid argument) */
+enum gdn2_status {
+  GDN2_OK = 0,
+  GDN2_ERR_NULL_POINTER = 1,
+  GDN2_ERR_SHAPE = 2,
+  GDN2_ERR_DTYPE = 3,
+  GDN2_ERR_UNSUPPORTED_DIM = 4, /* K or V not in {64, 128} */
+  GDN2_ERR_ALIGNMENT = 5,
+  GDN2_ERR_WORKSPACE = 6,       /* workspace pointer NULL or too small */
+  GDN2_ERR_FLAGS = 7,
+  GDN2_ERR_NO_DEVICE = 8
+};
+
+/* ------------------------------------------------------------------------- */
+/* chunkwise forward / backward                                              */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces the reference's chunk_gdn2 / ChunkGDN2Function
+ * (lit_gpt/gdn2_ops/chunk_gdn2.py:1363-1511 public API, :2504-2665 autograd)
+ * and the pipeline behind it: chunk_gdn2_fwd (:1205-1359), chunk_gdn2_bwd
+ * (:2330-2493), l2norm_fwd/bwd (:2542-2544, :2638-2640), the gate activation
+ * kda_gate_chunk_cumsum (chunk_kda.py:2636-2733) and kda_gate_bwd (:2420-2555).
+ */
+typedef struct gdn2_chunk_args {
+  int64_t B, T, H, K, V; /* q,k,g,b [B,T,H,K]; v,w,o [B,T,H,V] */
+  int64_t N;             /* number of sequences: B, or len(cu_seqlens)-1 */
+  int64_t NT;            /* total number of 64-token chunks over all sequences */
+  const int64_t* cu_seqlens;   /* [N+1] device, or NULL for dense [B,T] */
+  const int32_t* chunk_index;  /* [NT, 2] device (sequence, chunk-in-sequence) for varlen, else NULL */
+  const int32_t* chunk_offset; /* [N+1] device: first global chunk of each sequence (varlen), else NULL */
+  float scale;           /* attention scale (reference default K^-0.5) */
+  float lower_bound;     /* used with GDN2_LOWER_BOUND */
+  int32_t flags;         /* enum gdn2_flags */
+  int32_t dtype_qkv;     /* q, k, v, do and o: GDN2_BF16 */
+  int32_t dtype_bw;      /* b, w (and db, dw): GDN2_BF16 or GDN2_F32 */
+  const void* q;
+  const void* k;
+  const void* v;
+  const float* g;        /* log-decay (natural log), or the raw pre-activation */
+  const void* b;
+  const void* w;
+  const float* A_log;    /* [H]     with GDN2_GATE_IN_KERNEL */
+  const float* dt_bias;  /* [H*K]   optional with GDN2_GATE_IN_KERNEL */
+  const float* h0;       /* [N,H,K,V] fp32 with GDN2_HAS_H0 */
+  float* ht;             /* [N,H,K,V] fp32 with GDN2_STORE_FINAL */
+  void* o;               /* [B,T,H,V] dtype_qkv */
+} gdn2_chunk_args;
+
+typedef struct gdn2_chunk_grads {
+  const void* dout;      /* [B,T,H,V] dtype_qkv: cotangent of o */
+  const float* dht;      /* [N,H,K,V] fp32 cotangent of the final state, or NULL */
+  void* dq;              /* [B,T,H,K] dtype_qkv */
+  void* dk;              /* [B,T,H,K] dtype_qkv */
+  void* dv;              /* [B,T,H,V] dtype_qkv */
+  float* dg;             /* [B,T,H,K] fp32 (w.r.t. g as passed: raw when gated in kernel) */
+  void* db;              /* [B,T,H,K] dtype_bw */
+  void* dw;              /* [B,T,H,V] dtype_bw */
+  float* dh0;            /* [N,H,K,V] fp32 when GDN2_HAS_H0, else may be NULL */
+  float* dA_log;         /* [H] fp32 with GDN2_GATE_IN_KERNEL */
+  float* ddt_bias;       /* [H*K] fp32 with GDN2_GATE_IN_KERNEL and dt_bias */
+} gdn2_chunk_grads;
+
+/* Bytes of the forward->backward context: everything gdn2_chunk_fwd saves with
+ * GDN2_SAVE_FOR_BWD (normalised q/k, cumulative gates, WY factors, chunk
+ * states).  Without GDN2_SAVE_FOR_BWD only the forward's own scratch. */
+size_t gdn2_chunk_workspace_size(const gdn2_chunk_args* a);
+/* Bytes of additional scratch gdn2_chunk_bwd needs (state cotangents, dv). */
+size_t gdn2_chunk_bwd_workspace_size(const gdn2_chunk_args* a);
+
+int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* workspace, size_t workspace_bytes,
+                   gdn2_stream_t stream);
+/* `workspace` must hold what gdn2_chunk_fwd wrote with GDN2_SAVE_FOR_BWD for
+ * the same arguments. */
+int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr,
+                   const void* workspace, size_t workspace_bytes,
+                   void* bwd_workspace, size_t bwd_workspace_bytes, gdn2_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* token-serial recurrence (decode)                                          */
+/* ------------------------------------------------------------------------- */
+/*
+ * Replaces fused_recurrent_gdn2 / fused_recurrent_gdn2_fwd and its kernel
+ * (lit_gpt/gdn2_ops/fused_recurrent_gdn2.py:81-277 kernel, :284-395 launcher,
+ * :399-492 public API), including the serving features of the kernel:
+ * varlen (cu_seqlens), a paged state pool (ssm_state_indices), speculative
+ * decoding (num_accepted_tokens) and grouped value heads (HV a multiple of H).
+ */
+typedef struct gdn2_recurrent_args {
+  int64_t B, T, H, HV, K, V; /* q,k [B,T,H,K]; v,w,o [B,T,HV,V]; g,b [B,T,HV,K] */
+  int64_t N;                 /* sequences */
+  const int64_t* cu_seqlens; /* [N+1] or NULL */
+  const int32_t* ssm_state_indices; /* [N] or [N, stride_indices_seq] pool slots, or NULL */
+  const int32_t* num_accepted_tokens; /* [N] with ssm_state_indices (spec decoding), or NULL */
+  int64_t stride_indices_seq;  /* row stride of ssm_state_indices */
+  int64_t state_slot_stride_in;  /* elements between pool slots of h0 (default HV*K*V) */
+  int64_t state_slot_stride_out; /* elements between slots of ht (default HV*K*V) */
+  float scale;
+  float lower_bound;
+  int32_t flags;      /* GDN2_L2NORM_QK | GDN2_GATE_IN_KERNEL | GDN2_LOWER_BOUND |
+                         GDN2_TRANSPOSE_STATE | GDN2_HAS_H0 | GDN2_STORE_FINAL */
+  int32_t inplace;    /* with ssm_state_indices: write each token's state to its pool slot */
+  int32_t dtype_qkv;  /* q, k, v, o */
+  int32_t dtype_gbw;  /* g, b, w */
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* g;
+  const void* b;
+  const void* w;
+  const float* A_log;
+  const float* dt_bias;
+  const float* h0;    /* may alias ht (in-place update) */
+  float* ht;
+  void* o;
+} gdn2_recurrent_args;
+
+int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, gdn2_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* context parallel (T sharded over ranks)                                   */
+/* ------------------------------------------------------------------------- */
+/*
+ * A shard of one sequence maps its incoming state affinely:
+ *     S_out = M S_in + h_e,  M in R^{K x K}, h_e in R^{K x V}  (per head)
+ * gdn2_cp_transition computes [M | h_e] for a shard (gate activation, l2norm
+ * and the WY factors as in gdn2_chunk_fwd), packed as [H, K, K+V] fp32.  This
+ * mirrors the KDA context-parallel pre-process of the reference
+ * (chunk_kda.py:102-330 pre_process_fwd_kernel_merged, :774-852) which
+ * GDN2 shares the scan kernels with but never wires up (chunk_gdn2.py:86-92).
+ * gdn2_cp_compose folds the maps of ranks 0..rank-1 (gathered as
+ * [world, H, K, K+V]) into this rank's initial state (chunk_kda.py:465-477).
+ */
+int gdn2_cp_transition(const gdn2_chunk_args* a, float* maps, void* workspace,
+                       size_t workspace_bytes, gdn2_stream_t stream);
+int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t H, int64_t K, int64_t V,
+                    float* h0_out, gdn2_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+const char* gdn2_status_string(int status);
+/* 1 when the library was built for the running device (sm_100a present). */
+int gdn2_device_supported(int device);
+/* Version of this ABI (major*100 + minor). */
+int gdn2_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GDN2_B200_H_ */
