@@ -65,6 +65,10 @@ class RecurrentArgs(ctypes.Structure):
     ]
 
 
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("launches", _i64), ("total_ms", ctypes.c_double)]
+
+
 class Gdn2Error(RuntimeError):
     """A non-zero status from the C ABI."""
 
@@ -76,6 +80,7 @@ EXPORTS = (
     "gdn2_chunk_workspace_size", "gdn2_chunk_bwd_workspace_size", "gdn2_chunk_fwd",
     "gdn2_chunk_bwd", "gdn2_recurrent_fwd", "gdn2_cp_transition", "gdn2_cp_compose",
     "gdn2_status_string", "gdn2_device_supported", "gdn2_abi_version",
+    "gdn2_profile_enable", "gdn2_profile_read",
 )
 
 
@@ -108,6 +113,10 @@ def load() -> ctypes.CDLL:
     lib.gdn2_status_string.restype = ctypes.c_char_p
     lib.gdn2_device_supported.argtypes = [ctypes.c_int]
     lib.gdn2_device_supported.restype = ctypes.c_int
+    lib.gdn2_profile_enable.argtypes = [ctypes.c_int]
+    lib.gdn2_profile_enable.restype = ctypes.c_int
+    lib.gdn2_profile_read.argtypes = [ctypes.POINTER(KernelStat), ctypes.c_int]
+    lib.gdn2_profile_read.restype = ctypes.c_int
     lib.gdn2_abi_version.argtypes = []
     lib.gdn2_abi_version.restype = ctypes.c_int
     _lib = lib
@@ -144,3 +153,17 @@ def require_device(t: torch.Tensor) -> None:
         cap = torch.cuda.get_device_capability(idx)
         raise RuntimeError(f"libgdn2_b200 is built for sm_100a; device {idx} has capability {cap}")
     _checked_devices.add(idx)
+
+
+def profile_enable(on: bool) -> None:
+    """Start/stop recording per-launch CUDA-event timings inside the library."""
+    load().gdn2_profile_enable(1 if on else 0)
+
+
+def profile_read() -> dict:
+    """{kernel name: (launches, total device ms)} since the last read."""
+    buf = (KernelStat * 16)()
+    n = load().gdn2_profile_read(buf, 16)
+    if n < 0:
+        check(n, "gdn2_profile_read")
+    return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(n)}

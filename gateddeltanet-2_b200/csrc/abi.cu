@@ -9,7 +9,7 @@ namespace {
 
 bool dim_ok(int64_t d) { return d == 64 || d == 128; }
 
-int check_chunk(const gdn2_chunk_args* a, bool need_ptrs = true) {
+int check_chunk(const gdn2_chunk_args* a, bool need_ptrs = true, bool need_out = true) {
   if (!a) return GDN2_ERR_NULL_POINTER;
   if (a->B < 0 || a->T < 0 || a->H <= 0 || a->N < 0 || a->NT < 0) return GDN2_ERR_SHAPE;
   if (!dim_ok(a->K) || !dim_ok(a->V)) return GDN2_ERR_UNSUPPORTED_DIM;
@@ -24,12 +24,11 @@ int check_chunk(const gdn2_chunk_args* a, bool need_ptrs = true) {
   }
   if ((a->flags & GDN2_LOWER_BOUND) && !(a->flags & GDN2_GATE_IN_KERNEL)) return GDN2_ERR_FLAGS;
   if (!need_ptrs) return GDN2_OK;
-  if (a->B * a->T > 0 && (!a->q || !a->k || !a->v || !a->g || !a->b || !a->w || !a->o))
+  if (a->B * a->T > 0 && (!a->q || !a->k || !a->v || !a->g || !a->b || !a->w || (need_out && !a->o)))
     return GDN2_ERR_NULL_POINTER;
   if ((a->flags & GDN2_GATE_IN_KERNEL) && !a->A_log) return GDN2_ERR_NULL_POINTER;
-  if ((a->flags & GDN2_LOWER_BOUND) && !(a->flags & GDN2_GATE_IN_KERNEL)) return GDN2_ERR_FLAGS;
   if ((a->flags & GDN2_HAS_H0) && !a->h0) return GDN2_ERR_NULL_POINTER;
-  if ((a->flags & GDN2_STORE_FINAL) && !a->ht) return GDN2_ERR_NULL_POINTER;
+  if (need_out && (a->flags & GDN2_STORE_FINAL) && !a->ht) return GDN2_ERR_NULL_POINTER;
   // 16-byte alignment of the vectorised streams
   const void* ptrs[] = {a->q, a->k, a->v, a->b, a->w, a->o, a->g};
   for (const void* p : ptrs)
@@ -91,7 +90,7 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* workspace, size_t workspace_b
 int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr, const void* workspace,
                    size_t workspace_bytes, void* bwd_workspace, size_t bwd_workspace_bytes,
                    gdn2_stream_t stream) {
-  int st = check_chunk(a);
+  int st = check_chunk(a, true, false);  // the backward reads no o / ht
   if (st) return st;
   if (!(a->flags & GDN2_SAVE_FOR_BWD)) return GDN2_ERR_FLAGS;
   if (!gr || !gr->dout || !gr->dq || !gr->dk || !gr->dv || !gr->dg || !gr->db || !gr->dw)
@@ -123,7 +122,6 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, gdn2_stream_t stream) {
   if (a->B * a->T > 0 && (!a->q || !a->k || !a->v || !a->g || !a->b || !a->w || !a->o))
     return GDN2_ERR_NULL_POINTER;
   if ((a->flags & GDN2_GATE_IN_KERNEL) && !a->A_log) return GDN2_ERR_NULL_POINTER;
-  if ((a->flags & GDN2_LOWER_BOUND) && !(a->flags & GDN2_GATE_IN_KERNEL)) return GDN2_ERR_FLAGS;
   if ((a->flags & GDN2_HAS_H0) && !a->h0) return GDN2_ERR_NULL_POINTER;
   if ((a->flags & GDN2_STORE_FINAL) && !a->ht) return GDN2_ERR_NULL_POINTER;
   if (a->ssm_state_indices && !(a->flags & GDN2_STORE_FINAL)) return GDN2_ERR_FLAGS;

@@ -1,6 +1,726 @@
+// Chunkwise GDN2 backward (C = 64): the reference pipeline
+//   chunk_gdn2_bwd (lit_gpt/gdn2_ops/chunk_gdn2.py:2330-2493)
+//   = dAv (chunk_kda.py:3769-3831) -> dhu reverse scan (:1356-1669)
+//     -> gate-aware WY VJP (chunk_gdn2.py:1554-1735) -> intra VJP (:1759-2019)
+//     -> reverse cumsum of dg (:2477-2483) -> gate VJP (chunk_kda.py:2420-2555)
+//     -> l2norm VJP (chunk_gdn2.py:2638-2640)
+// as two B200 kernels.  The forward saved G, Aqk, A = (I+T)^-1, Y, kg, qg,
+// v_new and the per-chunk entering states h, so nothing is recomputed.
+//
+// chunk_scan_bwd_kernel (one CTA per (sequence, head, 64-column V tile)),
+// serial over chunks in reverse with the state cotangent dS [K x 64] in
+// tensor-core accumulators:
+//   dh[c]  = dS                                   (cotangent of the chunk's exit state)
+//   dv_new = Aqk^T do + kg dS
+//   dS    <- 2^G_last dS + scale qg^T do - Y^T dv_new
+//
+// chunk_bwd_intra_kernel (one CTA per (chunk, head)), everything else in one
+// pass with all [64 x K] accumulators (dq, dk, db, dG) in registers:
+//   dq  = scale (do h^T) 2^G + intra ;  dk = (v_new dh^T) 2^(G_last-G) + ...
+//   dY  = -dv_new h^T ;  d(w v) = A^T dv_new -> dv, dw
+//   dA  = dv_new (w v)^T + dY (b k 2^G)^T ;  dT = -A^T dA A^T (strictly lower)
+//   d(b k 2^G) = A^T dY -> db, dk, dG
+//   intra: dAqk = scale do v_new^T, dT through the anchored score factors
+//   (exact per-pair path for the (block, channel)s the forward flagged)
+//   dG -> in-chunk reverse cumsum -> gate VJP; l2norm VJP on dq, dk.
+#include "common.cuh"
 #include "chunk_layout.cuh"
+#include "profile.cuh"
+
 namespace gdn2 {
-int chunk_bwd_launch(const gdn2_chunk_args&, const gdn2_chunk_grads&, const ChunkWs&, const BwdWs&, cudaStream_t) {
-  return GDN2_ERR_FLAGS;
+
+GDN2_DEV void cp_async16b(void* dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(n));
 }
+GDN2_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+GDN2_DEV void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// ---------------------------------------------------------------------------
+// B2: reverse scan of the state cotangent
+// ---------------------------------------------------------------------------
+constexpr int kBScanThreads = 256;
+constexpr int kBScanBV = 64;
+
+template <int K>
+struct BScanStage {
+  static constexpr int LK = K + 8, LV = kBScanBV + 8, LA = kChunk + 8;
+  alignas(16) __nv_bfloat16 Y[kChunk][LK];
+  alignas(16) __nv_bfloat16 QG[kChunk][LK];
+  alignas(16) __nv_bfloat16 KG[kChunk][LK];
+  alignas(16) __nv_bfloat16 Aqk[kChunk][LA];
+  alignas(16) __nv_bfloat16 DO[kChunk][LV];
+  alignas(16) float glast[K];
+};
+
+template <int K>
+struct BScanSmem {
+  BScanStage<K> st[2];
+  alignas(16) __nv_bfloat16 DSb[K][kBScanBV + 8];
+  alignas(16) __nv_bfloat16 DV[kChunk][kBScanBV + 8];
+};
+
+template <int K, int V>
+GDN2_DEV void bscan_prefetch(BScanStage<K>& st, const ChunkWs& ws, const __nv_bfloat16* dout,
+                             const gdn2_chunk_args& a, int64_t t0, int L, int64_t h, int v0, int tid) {
+  const int64_t H = a.H;
+  for (int i = tid; i < kChunk * (K / 8); i += kBScanThreads) {
+    const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+    const bool ok = r < L;
+    const int64_t gi = ((t0 + (ok ? r : 0)) * H + h) * K + p;
+    cp_async16b(&st.Y[r][p], ws.Y + gi, ok);
+    cp_async16b(&st.QG[r][p], ws.qg + gi, ok);
+    cp_async16b(&st.KG[r][p], ws.kg + gi, ok);
+  }
+  for (int i = tid; i < kChunk * (kChunk / 8); i += kBScanThreads) {
+    const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
+    const bool ok = r < L;
+    cp_async16b(&st.Aqk[r][p], ws.Aqk + ((t0 + (ok ? r : 0)) * H + h) * kChunk + p, ok);
+  }
+  for (int i = tid; i < kChunk * (kBScanBV / 8); i += kBScanThreads) {
+    const int r = i / (kBScanBV / 8), p = (i % (kBScanBV / 8)) * 8;
+    const bool ok = r < L;
+    cp_async16b(&st.DO[r][p], dout + ((t0 + (ok ? r : 0)) * H + h) * V + v0 + p, ok);
+  }
+  for (int i = tid; i < K / 4; i += kBScanThreads)
+    cp_async16b(&st.glast[i * 4], ws.G + ((t0 + L - 1) * H + h) * K + i * 4, true);
 }
+
+template <int K, int V>
+__global__ void __launch_bounds__(kBScanThreads, 1)
+chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  BScanSmem<K>& sm = *reinterpret_cast<BScanSmem<K>*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t H = a.H;
+  const int v0 = blockIdx.x * kBScanBV;
+  const int64_t n = blockIdx.y / H, h = blockIdx.y % H;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t bos, len;
+  geo.seq(n, bos, len);
+  const int64_t nchunks = (len + kChunk - 1) / kChunk;
+  const int64_t c0 = geo.chunk0(n);
+  const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
+  const __nv_bfloat16* dout = static_cast<const __nv_bfloat16*>(gr.dout);
+
+  constexpr int kRowsPerWarp = K / 8;
+  constexpr int MT = kRowsPerWarp >= 16 ? kRowsPerWarp / 16 : 1;
+  constexpr int NT = kBScanBV / 8;
+  const bool srows = kRowsPerWarp >= 16;
+  const bool sown = srows || warp < 4;
+  const int sr0 = srows ? warp * kRowsPerWarp : warp * 16;
+  float dS[MT][NT][4];
+  acc_foreach(dS, sr0, 0, lane, [&](float& v, int r, int c) {
+    float x = 0.f;
+    if (sown && gr.dht) {
+      const float* d = gr.dht + (n * H + h) * (int64_t)K * V;
+      x = tr ? d[(int64_t)(v0 + c) * K + r] : d[(int64_t)r * V + v0 + c];
+    }
+    v = x;
+  });
+
+  auto chunk_len = [&](int64_t ci) {
+    const int64_t rem = len - ci * kChunk;
+    return (int)(rem < kChunk ? rem : kChunk);
+  };
+  if (nchunks > 0)
+    bscan_prefetch<K, V>(sm.st[(nchunks - 1) & 1], ws, dout, a, bos + (nchunks - 1) * kChunk,
+                         chunk_len(nchunks - 1), h, v0, tid);
+  cp_commit();
+
+  for (int64_t ci = nchunks - 1; ci >= 0; --ci) {
+    const int64_t t0 = bos + ci * kChunk;
+    const int L = chunk_len(ci);
+    BScanStage<K>& st = sm.st[ci & 1];
+    if (sown) {
+      acc_foreach(dS, sr0, 0, lane, [&](float& v, int r, int c) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(v);
+        sm.DSb[r][c] = b;
+        bw.dh[((c0 + ci) * H + h) * (int64_t)K * V + (int64_t)r * V + v0 + c] = b;
+      });
+    }
+    if (ci > 0) bscan_prefetch<K, V>(sm.st[(ci - 1) & 1], ws, dout, a, t0 - kChunk, chunk_len(ci - 1), h, v0, tid);
+    cp_commit();
+    cp_wait<1>();
+    __syncthreads();
+
+    // dv_new = Aqk^T do + kg dS      (warp tile 16 x 32)
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+    {
+      float acc[1][4][4];
+      zero_acc(acc);
+      warp_mma<1, 4, true, false>(acc, Smem{&st.Aqk[0][0], BScanStage<K>::LA}, m0,
+                                  Smem{&st.DO[0][0], BScanStage<K>::LV}, n0, 0, kChunk, lane);
+      warp_mma<1, 4, false, false>(acc, Smem{&st.KG[0][0], BScanStage<K>::LK}, m0,
+                                   Smem{&sm.DSb[0][0], kBScanBV + 8}, n0, 0, K, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(r < L ? v : 0.f);
+        sm.DV[r][c] = b;
+        if (r < L) bw.dvn[((t0 + r) * H + h) * V + v0 + c] = b;
+      });
+    }
+    __syncthreads();
+    // dS <- 2^G_last dS + scale qg^T do - Y^T dv_new
+    if (sown) {
+      float t1[MT][NT][4], t2[MT][NT][4];
+      zero_acc(t1);
+      zero_acc(t2);
+      warp_mma<MT, NT, true, false>(t1, Smem{&st.QG[0][0], BScanStage<K>::LK}, sr0,
+                                    Smem{&st.DO[0][0], BScanStage<K>::LV}, 0, 0, kChunk, lane);
+      warp_mma<MT, NT, true, false>(t2, Smem{&st.Y[0][0], BScanStage<K>::LK}, sr0,
+                                    Smem{&sm.DV[0][0], kBScanBV + 8}, 0, 0, kChunk, lane);
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int r = sr0 + 16 * i + (lane >> 2) + (e >> 1) * 8;
+            dS[i][j][e] = dS[i][j][e] * exp2_approx(st.glast[r]) + a.scale * t1[i][j][e] - t2[i][j][e];
+          }
+    }
+    __syncthreads();
+  }
+  cp_wait<0>();
+  if (sown && gr.dh0) {
+    float* d = gr.dh0 + (n * H + h) * (int64_t)K * V;
+    acc_foreach(dS, sr0, 0, lane, [&](float& v, int r, int c) {
+      if (tr) d[(int64_t)(v0 + c) * K + r] = v;
+      else d[(int64_t)r * V + v0 + c] = v;
+    });
+  }
+}
+
+// ---------------------------------------------------------------------------
+// B3: chunk-parallel WY + intra backward
+// ---------------------------------------------------------------------------
+constexpr int kBIntraThreads = 256;
+constexpr float kAnchorRangeB = 96.f;  // must match the forward's anchored range
+
+template <int K, int V>
+struct BIntraSmem {
+  static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 8;
+  alignas(16) float G[kChunk][K];          // later reused for dG
+  alignas(16) __nv_bfloat16 A[kChunk][LA];
+  alignas(16) __nv_bfloat16 DAqk[kChunk][LA];
+  alignas(16) __nv_bfloat16 DT[kChunk][LA];
+  alignas(16) float last[K];               // dgk_last + sum_r k dk_inter
+  alignas(16) float rsum[kChunk][2][2];    // l2norm row sums (q, k) per column half
+  alignas(16) uint8_t flag[4][K];
+  int nflag;
+  union alignas(128) {
+    struct {
+      alignas(16) __nv_bfloat16 DVN[kChunk][LV];
+      alignas(16) __nv_bfloat16 DY[kChunk][LK];
+      alignas(16) __nv_bfloat16 Hs[K][LV];
+      alignas(16) __nv_bfloat16 DH[K][LV];
+      alignas(16) __nv_bfloat16 DO[kChunk][LV];
+      alignas(16) __nv_bfloat16 VN[kChunk][LV];
+    } p1;
+    struct {
+      alignas(16) __nv_bfloat16 DVN[kChunk][LV];
+      alignas(16) __nv_bfloat16 DY[kChunk][LK];
+      alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
+      alignas(16) __nv_bfloat16 WV[kChunk][LV];
+      alignas(16) __nv_bfloat16 DA[kChunk][LA];
+      alignas(16) __nv_bfloat16 X[kChunk][LA];
+    } p2;
+    struct {
+      alignas(16) __nv_bfloat16 QG[kChunk][LK];
+      alignas(16) __nv_bfloat16 KBG[kChunk][LK];
+      alignas(16) __nv_bfloat16 KN[160][LK];
+    } p3;
+  } u;
+};
+
+using BIntraSmem128x128 = BIntraSmem<128, 128>;
+static_assert(offsetof(BIntraSmem128x128, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
+using BIntraSmem64x64 = BIntraSmem<64, 64>;
+static_assert(offsetof(BIntraSmem64x64, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
+using BScanSmem128 = BScanSmem<128>;
+static_assert(offsetof(BScanSmem128, DSb) % 16 == 0 && sizeof(BScanStage<128>) % 16 == 0, "stage alignment");
+
+template <typename TB>
+GDN2_DEV float ldb(const void* p, int64_t i) {
+  return to_f(static_cast<const TB*>(p)[i]);
+}
+
+template <int K, int V, typename TB>
+__global__ void __launch_bounds__(kBIntraThreads, 1)
+chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  using S = BIntraSmem<K, V>;
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t H = a.H, h = blockIdx.y, cglob = blockIdx.x;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t n, ci, bos, len;
+  geo.chunk(cglob, n, ci);
+  geo.seq(n, bos, len);
+  const int64_t t0 = bos + ci * kChunk;
+  const int64_t rem = len - ci * kChunk;
+  const int L = (int)(rem < kChunk ? rem : kChunk);
+  const int64_t cidx = geo.chunk0(n) + ci;
+  const float scale = a.scale;
+  const __nv_bfloat16* qn = ws.qn;
+  const __nv_bfloat16* kn = ws.kn;
+  const __nv_bfloat16* vin = static_cast<const __nv_bfloat16*>(a.v);
+  const __nv_bfloat16* dout = static_cast<const __nv_bfloat16*>(gr.dout);
+  auto tokK = [&](int r, int c) { return ((t0 + r) * H + h) * K + c; };
+  auto tokV = [&](int r, int c) { return ((t0 + r) * H + h) * V + c; };
+  auto qv = [&](int r, int c) { return r < L ? __bfloat162float(qn[tokK(r, c)]) : 0.f; };
+  auto kv = [&](int r, int c) { return r < L ? __bfloat162float(kn[tokK(r, c)]) : 0.f; };
+  auto bv = [&](int r, int c) { return r < L ? ldb<TB>(a.b, tokK(r, c)) : 0.f; };
+
+  // ---- loads -----------------------------------------------------------------
+  {
+    const __nv_bfloat16* hsrc = ws.h + (cidx * H + h) * (int64_t)K * V;
+    const __nv_bfloat16* dhsrc = bw.dh + (cidx * H + h) * (int64_t)K * V;
+    for (int i = tid; i < K * (V / 8); i += kBIntraThreads) {
+      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+      cp_async16b(&sm.u.p1.Hs[r][p], hsrc + (int64_t)r * V + p, true);
+      cp_async16b(&sm.u.p1.DH[r][p], dhsrc + (int64_t)r * V + p, true);
+    }
+    for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
+      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+      const bool ok = r < L;
+      const int64_t gi = tokV(ok ? r : 0, p);
+      cp_async16b(&sm.u.p1.DO[r][p], dout + gi, ok);
+      cp_async16b(&sm.u.p1.VN[r][p], ws.v_new + gi, ok);
+      cp_async16b(&sm.u.p1.DVN[r][p], bw.dvn + gi, ok);
+    }
+    for (int i = tid; i < kChunk * (kChunk / 8); i += kBIntraThreads) {
+      const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
+      const bool ok = r < L;
+      cp_async16b(&sm.A[r][p], ws.Akk + ((t0 + (ok ? r : 0)) * H + h) * kChunk + p, ok);
+    }
+    for (int i = tid; i < kChunk * (K / 4); i += kBIntraThreads) {
+      const int r = i / (K / 4), p = (i % (K / 4)) * 4;
+      const bool ok = r < L;
+      cp_async16b(&sm.G[r][p], ws.G + tokK(ok ? r : L - 1, p), true);  // padded rows repeat G_last
+    }
+    cp_commit();
+    for (int c = tid; c < K; c += kBIntraThreads) sm.last[c] = 0.f;
+    if (tid == 0) sm.nflag = 0;
+    cp_wait<0>();
+    __syncthreads();
+  }
+  // the forward's exactness flags (same criterion, same G)
+  for (int i = tid; i < 4 * K; i += kBIntraThreads) {
+    const int blk = i / K, c = i % K, a0 = blk * 16;
+    const int alast = min(a0 + 15, max(L - 1, 0));
+    const uint8_t f = (sm.G[a0][c] - sm.G[alast][c]) > kAnchorRangeB ? 1 : 0;
+    sm.flag[blk][c] = f;
+    if (f) atomicAdd(&sm.nflag, 1);
+  }
+
+  const int rb = warp & 3, ch = warp >> 2;
+  const int m0 = rb * 16;
+  constexpr int NTk = K / 16, NTv = V / 16;
+  const int n0 = ch * (K / 2), n0v = ch * (V / 2);
+  float dq[1][NTk][4], dk[1][NTk][4], db[1][NTk][4], dG[1][NTk][4];
+  zero_acc(dq);
+  zero_acc(dk);
+  zero_acc(db);
+  zero_acc(dG);
+  const float* Glast = &sm.G[kChunk - 1][0];
+
+  // ---- phase 1: products with h, dh ------------------------------------------
+  warp_mma<1, NTk, false, true>(dq, Smem{&sm.u.p1.DO[0][0], S::LV}, m0, Smem{&sm.u.p1.Hs[0][0], S::LV}, n0, 0, V,
+                                lane);
+  warp_mma<1, NTk, false, true>(dk, Smem{&sm.u.p1.VN[0][0], S::LV}, m0, Smem{&sm.u.p1.DH[0][0], S::LV}, n0, 0, V,
+                                lane);
+  {
+    float t[1][NTk][4];
+    zero_acc(t);
+    warp_mma<1, NTk, false, true>(t, Smem{&sm.u.p1.DVN[0][0], S::LV}, m0, Smem{&sm.u.p1.Hs[0][0], S::LV}, n0, 0, V,
+                                  lane);
+    acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { sm.u.p1.DY[r][c] = __float2bfloat16_rn(-v); });
+  }
+  // inter-chunk parts: dq = scale (do h^T) 2^G ; dk = (v_new dh^T) 2^(G_last - G)
+  {
+    float colsum[NTk][2];
+#pragma unroll
+    for (int j = 0; j < NTk; ++j) colsum[j][0] = colsum[j][1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        const float Gr = sm.G[r][c];
+        const float dqi = r < L ? dq[0][j][e] * scale * exp2_approx(Gr) : 0.f;
+        const float dki = r < L ? dk[0][j][e] * exp2_approx(Glast[c] - Gr) : 0.f;
+        dq[0][j][e] = dqi;
+        dk[0][j][e] = dki;
+        const float kk = kv(r, c);
+        dG[0][j][e] = qv(r, c) * dqi - kk * dki;
+        colsum[j][e & 1] += kk * dki;
+      }
+    // sum over the warp's 16 rows (lanes sharing lane&3), then across row blocks
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        float s = colsum[j][x];
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);
+        if (lane < 4) atomicAdd(&sm.last[n0 + 8 * j + 2 * lane + x], s);
+      }
+  }
+  // dgk_last = 2^G_last * sum_v h dh  (2 threads per state row)
+  {
+    const int r = tid >> 1, half = tid & 1;
+    float s = 0.f;
+    if (r < K) {
+      for (int v = half * (V / 2); v < (half + 1) * (V / 2); ++v)
+        s += __bfloat162float(sm.u.p1.Hs[r][v]) * __bfloat162float(sm.u.p1.DH[r][v]);
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (r < K && half == 0) atomicAdd(&sm.last[r], s * exp2_approx(Glast[r]));
+  }
+  // dAqk = scale do v_new^T (lower incl. diagonal)
+  {
+    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
+    float t[1][4][4];
+    zero_acc(t);
+    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p1.DO[0][0], S::LV}, mm, Smem{&sm.u.p1.VN[0][0], S::LV}, nn, 0, V,
+                                lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+      sm.DAqk[r][s] = __float2bfloat16_rn((s <= r && r < L) ? v * scale : 0.f);
+    });
+  }
+  // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv)
+  {
+    float t[1][NTv][4];
+    zero_acc(t);
+    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&sm.u.p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
+                                  lane);
+    __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
+    TB* dw = static_cast<TB*>(gr.dw);
+    acc_foreach(t, m0, n0v, lane, [&](float v, int r, int c) {
+      if (r < L) {
+        const int64_t gi = tokV(r, c);
+        dv[gi] = __float2bfloat16_rn(v * ldb<TB>(a.w, gi));
+        dw[gi] = from_f<TB>(v * __bfloat162float(vin[gi]));
+      }
+    });
+  }
+  __syncthreads();
+
+  // ---- phase 2: WY factors -----------------------------------------------------
+  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kBIntraThreads) {
+    float b8[8], k8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
+      b8[u] = bv(r, c);
+      k8[u] = kv(r, c);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
+      sm.u.p2.KB2G[r][c] = __float2bfloat16_rn(b8[u] * k8[u] * exp2_approx(sm.G[r][c]));
+    }
+  }
+  for (int i0 = tid; i0 < kChunk * V; i0 += 8 * kBIntraThreads) {
+    float w8[8], v8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
+      w8[u] = r < L ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
+      v8[u] = r < L ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
+      sm.u.p2.WV[r][c] = __float2bfloat16_rn(w8[u] * v8[u]);
+    }
+  }
+  __syncthreads();
+  {
+    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
+    float t[1][4][4];
+    zero_acc(t);
+    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DVN[0][0], S::LV}, mm, Smem{&sm.u.p2.WV[0][0], S::LV}, nn, 0, V,
+                                lane);
+    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DY[0][0], S::LK}, mm, Smem{&sm.u.p2.KB2G[0][0], S::LK}, nn, 0, K,
+                                lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+      sm.u.p2.DA[r][s] = __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
+    });
+  }
+  // d(b k 2^G) = A^T dY
+  {
+    float t[1][NTk][4];
+    zero_acc(t);
+    warp_mma<1, NTk, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&sm.u.p2.DY[0][0], S::LK}, n0, 0, kChunk,
+                                  lane);
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        if (r < L) {
+          const float ex = exp2_approx(sm.G[r][c]);
+          const float x = t[0][j][e] * ex;
+          const float bb = bv(r, c), kk = kv(r, c);
+          db[0][j][e] += kk * x;
+          dk[0][j][e] += bb * x;
+          dG[0][j][e] += bb * kk * x;
+        }
+      }
+  }
+  __syncthreads();
+  // dT = -A^T (dA A^T), strictly lower
+  {
+    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
+    float t[1][4][4];
+    zero_acc(t);
+    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) { sm.u.p2.X[r][s] = __float2bfloat16_rn(v); });
+    __syncthreads();
+    zero_acc(t);
+    warp_mma<1, 4, true, false>(t, Smem{&sm.A[0][0], S::LA}, mm, Smem{&sm.u.p2.X[0][0], S::LA}, nn, 0, kChunk, lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+      sm.DT[r][s] = __float2bfloat16_rn((s < r && r < L) ? -v : 0.f);
+    });
+  }
+  __syncthreads();
+
+  // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
+  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kBIntraThreads) {
+    float q8[8], k8[8], b8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
+      q8[u] = qv(r, c);
+      k8[u] = kv(r, c);
+      b8[u] = bv(r, c);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
+      const int blk = r >> 4, a0 = blk * 16;
+      const float kk = k8[u];
+      const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);
+      sm.u.p3.QG[r][c] = __float2bfloat16_rn(q8[u] * rowf);
+      sm.u.p3.KBG[r][c] = __float2bfloat16_rn(b8[u] * kk * rowf);
+      const float fd = sm.flag[blk][c] ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);
+      sm.u.p3.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kk * fd);
+      if (blk < 3) {
+        float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);
+        for (int ai = blk + 1; ai < 4; ++ai) {
+          if (ai > blk + 1) f *= exp2_approx(sm.G[ai * 16][c] - sm.G[ai * 16 - 16][c]);
+          sm.u.p3.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kk * f);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  {
+    // row parts: rows of block rb against columns [0, 16(rb+1))
+    float r1[1][NTk][4], r2[1][NTk][4];
+    zero_acc(r1);
+    zero_acc(r2);
+    Smem KNi{&sm.u.p3.KN[anchor_row0(rb)][0], S::LK};
+    warp_mma<1, NTk, false, false>(r1, Smem{&sm.DAqk[0][0], S::LA}, m0, KNi, n0, 0, 16 * (rb + 1), lane);
+    warp_mma<1, NTk, false, false>(r2, Smem{&sm.DT[0][0], S::LA}, m0, KNi, n0, 0, 16 * (rb + 1), lane);
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        const float rowf = exp2_approx(sm.G[r][c] - sm.G[m0][c]);
+        const float dqi = r1[0][j][e] * rowf;
+        const float rr = r2[0][j][e] * rowf;
+        const float kk = kv(r, c), bb = bv(r, c);
+        dq[0][j][e] += dqi;
+        dk[0][j][e] += rr * bb;
+        db[0][j][e] += rr * kk;
+        // the decay-gradient pieces use the very bf16 operands the MMAs read
+        // (QG = q 2^(G_r - G_a), KBG = b k 2^(G_r - G_a)), so that the row and
+        // column sides below cancel exactly when summed over the chunk.
+        dG[0][j][e] += __bfloat162float(sm.u.p3.QG[r][c]) * r1[0][j][e] +
+                       __bfloat162float(sm.u.p3.KBG[r][c]) * r2[0][j][e];
+      }
+  }
+  {
+    // column parts: this warp's rows as columns s of block rb, rows r of blocks >= rb
+    for (int ib = rb; ib < 4; ++ib) {
+      float cc[1][NTk][4];
+      zero_acc(cc);
+      warp_mma<1, NTk, true, false>(cc, Smem{&sm.DAqk[0][0], S::LA}, m0, Smem{&sm.u.p3.QG[0][0], S::LK}, n0, ib * 16,
+                                    ib * 16 + 16, lane);
+      warp_mma<1, NTk, true, false>(cc, Smem{&sm.DT[0][0], S::LA}, m0, Smem{&sm.u.p3.KBG[0][0], S::LK}, n0, ib * 16,
+                                    ib * 16 + 16, lane);
+#pragma unroll
+      for (int j = 0; j < NTk; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int s = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+          float cf = exp2_approx(sm.G[ib * 16][c] - sm.G[s][c]);
+          if (ib == rb && sm.flag[rb][c]) cf = 0.f;
+          dk[0][j][e] += cc[0][j][e] * cf;
+          // KN_ib[s] = bf16(k_s 2^(G_a - G_s)): the row side's operand
+          dG[0][j][e] -= __bfloat162float(sm.u.p3.KN[anchor_row0(ib) + s][c]) * cc[0][j][e];
+        }
+    }
+  }
+  // exact per-pair contributions of flagged (block, channel)s
+  if (sm.nflag > 0) {
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        if (!sm.flag[rb][c] || r >= L) continue;
+        const float Gr = sm.G[r][c], qr = qv(r, c), kr = kv(r, c), br = bv(r, c);
+        float dqi = 0.f, rr = 0.f, col = 0.f;
+        for (int s = m0; s <= r; ++s) {
+          const float E = exp2f(Gr - sm.G[s][c]);
+          const float ks = kv(s, c);
+          dqi += __bfloat162float(sm.DAqk[r][s]) * ks * E;
+          if (s < r) rr += __bfloat162float(sm.DT[r][s]) * ks * E;
+        }
+        const int rend = (m0 + 16 < L) ? m0 + 16 : L;
+        for (int r2 = r; r2 < rend; ++r2) {
+          const float E = exp2f(sm.G[r2][c] - Gr);
+          col += (__bfloat162float(sm.DAqk[r2][r]) * qv(r2, c) +
+                  __bfloat162float(sm.DT[r2][r]) * bv(r2, c) * kv(r2, c)) * E;
+        }
+        dq[0][j][e] += dqi;
+        dk[0][j][e] += rr * br + col;
+        db[0][j][e] += rr * kr;
+        dG[0][j][e] += qr * dqi + kr * br * rr - kr * col;
+      }
+  }
+  __syncthreads();  // every read of G is done: its buffer becomes dG
+
+  // ---- phase 4: epilogue -------------------------------------------------------
+  const bool l2 = a.flags & GDN2_L2NORM_QK;
+  {
+    float pq[2] = {0.f, 0.f}, pk[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        float g = dG[0][j][e];
+        if (r == L - 1) g += sm.last[c];
+        sm.G[r][c] = r < L ? g : 0.f;
+        pq[e >> 1] += dq[0][j][e] * qv(r, c);
+        pk[e >> 1] += dk[0][j][e] * kv(r, c);
+      }
+    if (l2) {
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        pq[x] += __shfl_xor_sync(0xffffffffu, pq[x], 1);
+        pq[x] += __shfl_xor_sync(0xffffffffu, pq[x], 2);
+        pk[x] += __shfl_xor_sync(0xffffffffu, pk[x], 1);
+        pk[x] += __shfl_xor_sync(0xffffffffu, pk[x], 2);
+      }
+      if ((lane & 3) == 0) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          sm.rsum[m0 + (lane >> 2) + 8 * x][ch][0] = pq[x];
+          sm.rsum[m0 + (lane >> 2) + 8 * x][ch][1] = pk[x];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  {
+    __nv_bfloat16* dqo = static_cast<__nv_bfloat16*>(gr.dq);
+    __nv_bfloat16* dko = static_cast<__nv_bfloat16*>(gr.dk);
+    TB* dbo = static_cast<TB*>(gr.db);
+#pragma unroll
+    for (int j = 0; j < NTk; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        if (r >= L) continue;
+        const int64_t gi = tokK(r, c);
+        float xq = dq[0][j][e], xk = dk[0][j][e];
+        if (l2) {
+          const float sq = sm.rsum[r][0][0] + sm.rsum[r][1][0];
+          const float sk = sm.rsum[r][0][1] + sm.rsum[r][1][1];
+          const float rq = ws.q_rstd[(t0 + r) * H + h], rk = ws.k_rstd[(t0 + r) * H + h];
+          xq = (xq - sq * qv(r, c)) * rq;
+          xk = (xk - sk * kv(r, c)) * rk;
+        }
+        dqo[gi] = __float2bfloat16_rn(xq);
+        dko[gi] = __float2bfloat16_rn(xk);
+        dbo[gi] = from_f<TB>(db[0][j][e]);
+      }
+  }
+  // dg: reverse cumsum inside the chunk, then the gate VJP
+  const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
+  const bool lbnd = a.flags & GDN2_LOWER_BOUND;
+  for (int c = tid; c < K; c += kBIntraThreads) {
+    const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
+    const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
+    float acc = 0.f, dA = 0.f, dbias = 0.f;
+    for (int r = L - 1; r >= 0; --r) {
+      acc += sm.G[r][c];
+      const int64_t gi = tokK(r, c);
+      float out = acc;
+      if (gate) {
+        const float x = a.g[gi] + bias;
+        if (lbnd) {
+          const float sg = sigmoid_f(Aexp * x);
+          out = acc * a.lower_bound * sg * (1.f - sg) * Aexp;
+          dA += out * x;
+        } else {
+          out = -Aexp * acc * sigmoid_f(x);
+          dA += acc * (-Aexp * softplus_f(x));
+        }
+        dbias += out;
+      }
+      gr.dg[gi] = out;
+    }
+    if (gate) {
+      if (a.dt_bias) atomicAdd(&gr.ddt_bias[h * K + c], dbias);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dA += __shfl_xor_sync(0xffffffffu, dA, off);
+      if ((c & 31) == 0) atomicAdd(&gr.dA_log[h], dA);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int K, int V>
+int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                  cudaStream_t s) {
+  const size_t sm2 = sizeof(BScanSmem<K>);
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_bwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sm2));
+  dim3 g2((unsigned)(V / kBScanBV), (unsigned)(a.N * a.H));
+  {
+    ProfScope ps(kKScanBwd, s);
+    chunk_scan_bwd_kernel<K, V><<<g2, kBScanThreads, sm2, s>>>(a, g, ws, bw);
+  }
+  GDN2_LAUNCH_CHECK();
+  if (a.NT > 0) {
+    const size_t sm3 = sizeof(BIntraSmem<K, V>);
+    auto k3 = a.dtype_bw == GDN2_BF16 ? chunk_bwd_intra_kernel<K, V, __nv_bfloat16>
+                                      : chunk_bwd_intra_kernel<K, V, float>;
+    GDN2_CUDA_TRY(cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3));
+    dim3 g3((unsigned)a.NT, (unsigned)a.H);
+    ProfScope ps(kKBwdIntra, s);
+    k3<<<g3, kBIntraThreads, sm3, s>>>(a, g, ws, bw);
+    GDN2_LAUNCH_CHECK();
+  }
+  return 0;
+}
+
+int chunk_bwd_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                     cudaStream_t s) {
+  if (a.K == 128 && a.V == 128) return launch_bwd_kv<128, 128>(a, g, ws, bw, s);
+  if (a.K == 128 && a.V == 64) return launch_bwd_kv<128, 64>(a, g, ws, bw, s);
+  if (a.K == 64 && a.V == 128) return launch_bwd_kv<64, 128>(a, g, ws, bw, s);
+  return launch_bwd_kv<64, 64>(a, g, ws, bw, s);
+}
+
+}  // namespace gdn2

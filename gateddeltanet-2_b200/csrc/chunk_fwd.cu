@@ -32,41 +32,55 @@
 //   chunk computes.
 #include "common.cuh"
 #include "chunk_layout.cuh"
+#include "profile.cuh"
 
 namespace gdn2 {
 
 // ---------------------------------------------------------------------------
 // F1: chunk-parallel intra kernel
 // ---------------------------------------------------------------------------
+GDN2_DEV void cp_async16(void* dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(n));
+}
+GDN2_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+GDN2_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
 constexpr float kAnchorRange = 96.f;  // max log2 decay range kept on the tensor-core path
 constexpr int kIntraThreads = 256;
 
 template <int K, int V>
 struct IntraSmem {
   static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 4, LAB = kChunk + 8;
-  float G[kChunk][K];
-  __nv_bfloat16 Q[kChunk][LK];
-  __nv_bfloat16 Kt[kChunk][LK];
-  float Aqk[kChunk][LA];
-  float Tm[kChunk][LA];
-  float Af[kChunk][LA];
-  __nv_bfloat16 Ab[kChunk][LAB];
-  union {
+  alignas(16) float G[kChunk][K];
+  alignas(16) __nv_bfloat16 Q[kChunk][LK];
+  alignas(16) __nv_bfloat16 Kt[kChunk][LK];
+  alignas(16) float Aqk[kChunk][LA];
+  alignas(16) float Tm[kChunk][LA];
+  alignas(16) float Af[kChunk][LA];
+  alignas(16) __nv_bfloat16 Ab[kChunk][LAB];
+  union alignas(128) {
     struct {
-      __nv_bfloat16 QG[kChunk][LK];
-      __nv_bfloat16 KBG[kChunk][LK];
-      __nv_bfloat16 KN[160][LK];  // anchors 0..3: rows [0,16), [16,48), [48,96), [96,160)
+      alignas(16) __nv_bfloat16 QG[kChunk][LK];
+      alignas(16) __nv_bfloat16 KBG[kChunk][LK];
+      alignas(16) __nv_bfloat16 KN[160][LK];  // anchors 0..3: rows [0,16), [16,48), [48,96), [96,160)
     } s;
     struct {
-      __nv_bfloat16 KB2G[kChunk][LK];
-      __nv_bfloat16 WV[kChunk][LV];
+      alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
+      alignas(16) __nv_bfloat16 WV[kChunk][LV];
     } w;
   } u;
-  float P[4][16][17];        // solve scratch
-  float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
-  uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
+  alignas(16) float P[4][16][17];        // solve scratch
+  alignas(16) float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
+  alignas(16) uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
   int nflag[4];
 };
+
+using IntraSmem128x128 = IntraSmem<128, 128>;
+static_assert(offsetof(IntraSmem128x128, u) % 128 == 0, "ldmatrix targets need 16B alignment");
+using IntraSmem64x64 = IntraSmem<64, 64>;
+static_assert(offsetof(IntraSmem64x64, u) % 128 == 0, "ldmatrix targets need 16B alignment");
 
 template <typename TB>
 GDN2_DEV float ld_bw(const void* p, int64_t i) {
@@ -95,84 +109,84 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   const __nv_bfloat16* kin = static_cast<const __nv_bfloat16*>(a.k);
   const __nv_bfloat16* vin = static_cast<const __nv_bfloat16*>(a.v);
 
-  // ---- 1. q, k rows (+ l2norm) ---------------------------------------------
-  // warp w owns rows 8w..8w+7; lane owns channels lane, lane+32, ...
-  for (int rr = 0; rr < 8; ++rr) {
-    const int r = warp * 8 + rr;
-    float qv[K / 32], kv[K / 32];
-    float sq = 0.f, sk = 0.f;
+  // ---- 1. stage q, k (bf16) and raw g (fp32) with cp.async; l2norm in smem -
+  for (int i = tid; i < kChunk * (K / 8); i += kIntraThreads) {
+    const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+    const bool ok = r < L;
+    const int64_t gi = ((t0 + (ok ? r : 0)) * H + h) * K + p;
+    cp_async16(&sm.Q[r][p], qin + gi, ok);
+    cp_async16(&sm.Kt[r][p], kin + gi, ok);
+  }
+  for (int i = tid; i < kChunk * (K / 4); i += kIntraThreads) {
+    const int r = i / (K / 4), p = (i % (K / 4)) * 4;
+    const bool ok = r < L;
+    cp_async16(&sm.G[r][p], a.g + ((t0 + (ok ? r : 0)) * H + h) * K + p, ok);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  if (l2) {
+    // warp w owns rows 8w..8w+7; lane owns channels lane, lane+32, ...
+    for (int rr = 0; rr < 8; ++rr) {
+      const int r = warp * 8 + rr;
+      float qv[K / 32], kv[K / 32];
+      float sq = 0.f, sk = 0.f;
 #pragma unroll
-    for (int j = 0; j < K / 32; ++j) {
-      const int c = lane + 32 * j;
-      if (r < L) {
-        const int64_t idx = ((t0 + r) * H + h) * K + c;
-        qv[j] = to_f(qin[idx]);
-        kv[j] = to_f(kin[idx]);
-      } else {
-        qv[j] = 0.f;
-        kv[j] = 0.f;
+      for (int j = 0; j < K / 32; ++j) {
+        qv[j] = __bfloat162float(sm.Q[r][lane + 32 * j]);
+        kv[j] = __bfloat162float(sm.Kt[r][lane + 32 * j]);
+        sq += qv[j] * qv[j];
+        sk += kv[j] * kv[j];
       }
-      sq += qv[j] * qv[j];
-      sk += kv[j] * kv[j];
-    }
-    float rq = 1.f, rk = 1.f;
-    if (l2) {
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
         sq += __shfl_xor_sync(0xffffffffu, sq, off);
         sk += __shfl_xor_sync(0xffffffffu, sk, off);
       }
-      rq = rsqrtf(sq + kL2Eps);
-      rk = rsqrtf(sk + kL2Eps);
+      const float rq = rsqrtf(sq + kL2Eps), rk = rsqrtf(sk + kL2Eps);
       if (save && r < L && lane == 0) {
         ws.q_rstd[(t0 + r) * H + h] = rq;
         ws.k_rstd[(t0 + r) * H + h] = rk;
       }
-    }
 #pragma unroll
-    for (int j = 0; j < K / 32; ++j) {
-      const int c = lane + 32 * j;
-      const __nv_bfloat16 qb = __float2bfloat16_rn(qv[j] * rq);
-      const __nv_bfloat16 kb = __float2bfloat16_rn(kv[j] * rk);
-      sm.Q[r][c] = qb;
-      sm.Kt[r][c] = kb;
-      if (l2 && save && r < L) {
-        const int64_t idx = ((t0 + r) * H + h) * K + c;
-        ws.qn[idx] = qb;
-        ws.kn[idx] = kb;
+      for (int j = 0; j < K / 32; ++j) {
+        sm.Q[r][lane + 32 * j] = __float2bfloat16_rn(qv[j] * rq);
+        sm.Kt[r][lane + 32 * j] = __float2bfloat16_rn(kv[j] * rk);
       }
     }
   }
 
-  // ---- 2. gate activation + chunk-local cumsum (log2 units) ----------------
+  // ---- 2. gate activation + chunk-local cumsum (log2 units), in smem --------
   const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
   const bool lbnd = a.flags & GDN2_LOWER_BOUND;
   for (int c = tid; c < K; c += kIntraThreads) {
     const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
     const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
     float Gc = 0.f;
-    for (int r0 = 0; r0 < kChunk; r0 += 8) {
-      float gv[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + j;
-        gv[j] = r < L ? a.g[((t0 + r) * H + h) * K + c] : 0.f;
+    for (int r = 0; r < kChunk; ++r) {
+      float x = sm.G[r][c];
+      if (gate) {
+        x += bias;
+        x = lbnd ? a.lower_bound * sigmoid_f(Aexp * x) : -Aexp * softplus_f(x);
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = r0 + j;
-        float x = gv[j];
-        if (gate) {
-          x += bias;
-          x = lbnd ? a.lower_bound * sigmoid_f(Aexp * x) : -Aexp * softplus_f(x);
-        }
-        if (r < L) Gc += x * kRcpLn2;
-        sm.G[r][c] = Gc;  // padded rows repeat G_last
-        if (r < L) ws.G[((t0 + r) * H + h) * K + c] = Gc;
-      }
+      if (r < L) Gc += x * kRcpLn2;
+      sm.G[r][c] = Gc;  // padded rows repeat G_last
     }
   }
   __syncthreads();
+  // vectorised copies of G (and the normalised q, k) to the workspace
+  for (int i = tid; i < L * (K / 4); i += kIntraThreads) {
+    const int r = i / (K / 4), p = (i % (K / 4)) * 4;
+    *reinterpret_cast<float4*>(ws.G + ((t0 + r) * H + h) * K + p) = *reinterpret_cast<const float4*>(&sm.G[r][p]);
+  }
+  if (l2 && save) {
+    for (int i = tid; i < L * (K / 8); i += kIntraThreads) {
+      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+      const int64_t gi = ((t0 + r) * H + h) * K + p;
+      *reinterpret_cast<uint4*>(ws.qn + gi) = *reinterpret_cast<const uint4*>(&sm.Q[r][p]);
+      *reinterpret_cast<uint4*>(ws.kn + gi) = *reinterpret_cast<const uint4*>(&sm.Kt[r][p]);
+    }
+  }
 
   // ---- 3. anchored tensor-core operands ------------------------------------
   for (int i = tid; i < 4 * K; i += kIntraThreads) {
@@ -188,26 +202,33 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   for (int i = tid; i < 4 * K; i += kIntraThreads) {
     if (sm.flag[i / K][i % K]) atomicAdd(&sm.nflag[i / K], 1);
   }
-  for (int i = tid; i < kChunk * K; i += kIntraThreads) {
-    const int r = i / K, c = i % K;
-    const int blk = r >> 4, a0 = blk * 16;
-    const float kq = __bfloat162float(sm.Kt[r][c]);
-    const float qq = __bfloat162float(sm.Q[r][c]);
-    const float bb = r < L ? ((a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.b, ((t0 + r) * H + h) * K + c)
-                                                      : ld_bw<float>(a.b, ((t0 + r) * H + h) * K + c))
-                           : 0.f;
-    const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);  // <= 1
-    sm.u.s.QG[r][c] = __float2bfloat16_rn(qq * rowf);
-    sm.u.s.KBG[r][c] = __float2bfloat16_rn(bb * kq * rowf);
-    // column operands for every anchor at or after this row's block
-    const bool fl = sm.flag[blk][c];
-    const float fd = fl ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);  // >= 1, bounded
-    sm.u.s.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kq * fd);
-    if (blk < 3) {
-      float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);  // <= 1
-      for (int ai = blk + 1; ai < 4; ++ai) {
-        if (ai > blk + 1) f *= sm.Dblk[ai][c];
-        sm.u.s.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kq * f);
+  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kIntraThreads) {
+    float bv8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+      bv8[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+      const int blk = r >> 4, a0 = blk * 16;
+      const float kq = __bfloat162float(sm.Kt[r][c]);
+      const float qq = __bfloat162float(sm.Q[r][c]);
+      const float bb = bv8[u];
+      const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);  // <= 1
+      sm.u.s.QG[r][c] = __float2bfloat16_rn(qq * rowf);
+      sm.u.s.KBG[r][c] = __float2bfloat16_rn(bb * kq * rowf);
+      // column operands for every anchor at or after this row's block
+      const bool fl = sm.flag[blk][c];
+      const float fd = fl ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);  // >= 1, bounded
+      sm.u.s.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kq * fd);
+      if (blk < 3) {
+        float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);  // <= 1
+        for (int ai = blk + 1; ai < 4; ++ai) {
+          if (ai > blk + 1) f *= sm.Dblk[ai][c];
+          sm.u.s.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kq * f);
+        }
       }
     }
   }
@@ -329,31 +350,42 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   }
   // WY operands (the score operands are dead now)
   __syncthreads();
-  for (int i = tid; i < kChunk * K; i += kIntraThreads) {
-    const int r = i / K, c = i % K;
-    const float bb = r < L ? ((a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.b, ((t0 + r) * H + h) * K + c)
-                                                      : ld_bw<float>(a.b, ((t0 + r) * H + h) * K + c))
-                           : 0.f;
-    const float kq = __bfloat162float(sm.Kt[r][c]);
-    const float qq = __bfloat162float(sm.Q[r][c]);
-    const float Gr = sm.G[r][c];
-    const float e = exp2_approx(Gr);
-    sm.u.w.KB2G[r][c] = __float2bfloat16_rn(bb * kq * e);
-    if (r < L) {
-      const int64_t gi = ((t0 + r) * H + h) * K + c;
-      ws.kg[gi] = __float2bfloat16_rn(kq * exp2_approx(sm.G[kChunk - 1][c] - Gr));
-      ws.qg[gi] = __float2bfloat16_rn(qq * e);
+  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kIntraThreads) {
+    float bv8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+      bv8[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+      const float kq = __bfloat162float(sm.Kt[r][c]);
+      const float qq = __bfloat162float(sm.Q[r][c]);
+      const float Gr = sm.G[r][c];
+      const float e = exp2_approx(Gr);
+      sm.u.w.KB2G[r][c] = __float2bfloat16_rn(bv8[u] * kq * e);
+      if (r < L) {
+        const int64_t gi = ((t0 + r) * H + h) * K + c;
+        ws.kg[gi] = __float2bfloat16_rn(kq * exp2_approx(sm.G[kChunk - 1][c] - Gr));
+        ws.qg[gi] = __float2bfloat16_rn(qq * e);
+      }
     }
   }
-  for (int i = tid; i < kChunk * V; i += kIntraThreads) {
-    const int r = i / V, c = i % V;
-    float wv = 0.f;
-    if (r < L) {
+  for (int i0 = tid; i0 < kChunk * V; i0 += 8 * kIntraThreads) {
+    float wv8[8], vv8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / V, c = i % V;
       const int64_t gi = ((t0 + r) * H + h) * V + c;
-      const float ww = (a.dtype_bw == GDN2_BF16) ? ld_bw<__nv_bfloat16>(a.w, gi) : ld_bw<float>(a.w, gi);
-      wv = ww * __bfloat162float(vin[gi]);
+      wv8[u] = r < L ? ld_bw<TB>(a.w, gi) : 0.f;
+      vv8[u] = r < L ? __bfloat162float(vin[gi]) : 0.f;
     }
-    sm.u.w.WV[r][c] = __float2bfloat16_rn(wv);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kIntraThreads, r = i / V, c = i % V;
+      sm.u.w.WV[r][c] = __float2bfloat16_rn(wv8[u] * vv8[u]);
+    }
   }
   __syncthreads();
 
@@ -394,28 +426,20 @@ constexpr int kScanBV = 64;
 template <int K>
 struct ScanStage {
   static constexpr int LK = K + 8, LV = kScanBV + 8, LA = kChunk + 8;
-  __nv_bfloat16 Y[kChunk][LK];
-  __nv_bfloat16 QG[kChunk][LK];
-  __nv_bfloat16 KG[kChunk][LK];
-  __nv_bfloat16 Aqk[kChunk][LA];
-  __nv_bfloat16 U[kChunk][LV];
-  float glast[K];
+  alignas(16) __nv_bfloat16 Y[kChunk][LK];
+  alignas(16) __nv_bfloat16 QG[kChunk][LK];
+  alignas(16) __nv_bfloat16 KG[kChunk][LK];
+  alignas(16) __nv_bfloat16 Aqk[kChunk][LA];
+  alignas(16) __nv_bfloat16 U[kChunk][LV];
+  alignas(16) float glast[K];
 };
 
 template <int K>
 struct ScanSmem {
   ScanStage<K> st[2];
-  __nv_bfloat16 Sb[K][kScanBV + 8];      // bf16 copy of the state (MMA operand)
-  __nv_bfloat16 VN[kChunk][kScanBV + 8]; // v_new (bf16)
+  alignas(16) __nv_bfloat16 Sb[K][kScanBV + 8];      // bf16 copy of the state (MMA operand)
+  alignas(16) __nv_bfloat16 VN[kChunk][kScanBV + 8]; // v_new (bf16)
 };
-
-GDN2_DEV void cp_async16(void* dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(n));
-}
-GDN2_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-GDN2_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 template <int K, int V>
 GDN2_DEV void scan_prefetch(ScanStage<K>& st, const ChunkWs& ws, const gdn2_chunk_args& a, int64_t t0, int L,
@@ -564,6 +588,7 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
     auto k1 = a.dtype_bw == GDN2_BF16 ? chunk_intra_kernel<K, V, __nv_bfloat16> : chunk_intra_kernel<K, V, float>;
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
     dim3 g1((unsigned)a.NT, (unsigned)a.H);
+    ProfScope ps(kKIntra, s);
     k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
     GDN2_LAUNCH_CHECK();
   }
@@ -571,6 +596,7 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
   GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)sm2));
   dim3 g2((unsigned)(V / kScanBV), (unsigned)(a.N * a.H));
+  ProfScope ps(kKScanFwd, s);
   chunk_scan_fwd_kernel<K, V><<<g2, kScanThreads, sm2, s>>>(a, ws);
   GDN2_LAUNCH_CHECK();
   return 0;

@@ -10,6 +10,7 @@
 // of the same pass over the tile: warp shuffles, then a cross-warp smem step.
 // o uses S_new^T q = S_dec^T q + u (k.q), so the state is touched once per token.
 #include "common.cuh"
+#include "profile.cuh"
 
 namespace gdn2 {
 
@@ -241,6 +242,7 @@ template <typename TQ, typename TG, int K>
 cudaError_t launch_rec(const gdn2_recurrent_args& a, cudaStream_t s) {
   const int64_t grid = a.N * a.HV * (a.V / kRecBV);
   if (grid == 0) return cudaSuccess;
+  ProfScope ps(kKRecurrent, s);
   if (a.flags & GDN2_TRANSPOSE_STATE)
     recurrent_kernel<TQ, TG, K, true><<<(unsigned)grid, kRecThreads, 0, s>>>(a);
   else

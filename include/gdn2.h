@@ -194,6 +194,21 @@ int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t H, int64_t
                     float* h0_out, gdn2_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* opt-in per-kernel timing (measurement hook, no reference counterpart)     */
+/* ------------------------------------------------------------------------- */
+/* While enabled, every launch of the library is bracketed by CUDA events on
+ * its stream.  gdn2_profile_read waits for the recorded launches, writes up
+ * to max_entries {kernel name, launches, total device ms} records, clears the
+ * record and returns how many it wrote (< 0: CUDA error). */
+typedef struct gdn2_kernel_stat {
+  const char* name;
+  int64_t launches;
+  double total_ms;
+} gdn2_kernel_stat;
+int gdn2_profile_enable(int on);
+int gdn2_profile_read(gdn2_kernel_stat* out, int max_entries);
+
+/* ------------------------------------------------------------------------- */
 const char* gdn2_status_string(int status);
 /* 1 when the library was built for the running device (sm_100a present). */
 int gdn2_device_supported(int device);

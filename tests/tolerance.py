@@ -31,3 +31,28 @@ def assert_close(actual, expected, name="", rtol=RTOL, atol=ATOL):
 
 def max_err(actual, expected):
     return float(np.abs(to_np(actual) - to_np(expected)).max())
+
+
+def gate_param_masses(g_raw, dt_bias, dg_raw, H):
+    """Summed magnitudes of the terms that the A_log and dt_bias gradients add
+    up: dA_log[h] = sum_{t,c} dy*yg and ddt_bias[h,c] = sum_t dg_raw, with
+    |dy*yg| = |dg_raw| * softplus(x) / sigmoid(x), x = g + dt_bias.  A bound on
+    a sum of N rounded terms scales with this mass, not with the sum itself."""
+    g = to_np(g_raw)
+    K = g.shape[-1]
+    x = g + (to_np(dt_bias).reshape(H, K) if dt_bias is not None else 0.0)
+    sp = np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20))))
+    sg = 1.0 / (1.0 + np.exp(-x))
+    d = np.abs(to_np(dg_raw))
+    mA = (d * sp / sg).reshape(-1, H, K).sum((0, 2))
+    mdt = d.reshape(-1, H * K).sum(0)
+    return mA, mdt
+
+
+def assert_close_reduced(actual, expected, mass, name="", rtol=RTOL, atol=ATOL):
+    """Parity for a gradient that is a sum of many terms: |x - ref| <= atol + rtol * sum|terms|."""
+    a, e, m = to_np(actual), to_np(expected), to_np(mass)
+    err = np.abs(a - e)
+    bad = err > atol + rtol * m
+    assert not bad.any(), (f"{name}: {int(bad.sum())}/{bad.size} out of tolerance; max abs err "
+                           f"{err.max():.3e}, bound {float((atol + rtol * m).min()):.3e}")
