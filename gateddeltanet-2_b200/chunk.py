@@ -284,3 +284,12 @@ def chunk_gdn2(
         safe_gate, lower_bound, disable_recompute, return_intermediate_states,
         transpose_state_layout,
     )
+
+
+def gdn2_telemetry_snapshot(reset: bool = True) -> dict:
+    """Interface twin of the reference's ``gdn2_telemetry_snapshot``
+    (``chunk_gdn2.py:134-153``), which trainers import next to ``chunk_gdn2``.
+    The reference collects gate-range maxima to drive its anchored-clamp guard;
+    this operator is exact for any gate range and keeps no such statistics, so
+    the snapshot is always empty."""
+    return {}

@@ -1,0 +1,86 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol
+include/gdn2.h declares, and rejects invalid arguments before any launch."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_header_symbols_are_exported(gdn2):
+    lib = gdn2._lib.load()
+    with open(os.path.join(ROOT, "include", "gdn2.h")) as f:
+        hdr = f.read()
+    declared = set(re.findall(r"\b(gdn2_\w+)\s*\(", hdr))
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in gdn2.h but not exported"
+    assert set(gdn2._lib.EXPORTS) <= declared
+
+
+def test_status_strings_and_version(gdn2):
+    lib = gdn2._lib.load()
+    assert lib.gdn2_abi_version() >= 100
+    assert b"aligned" in lib.gdn2_status_string(5)
+    assert lib.gdn2_status_string(0) == b"ok"
+
+
+def _args(gdn2, **kw):
+    a = dict(B=4, T=4096, H=16, K=128, V=128, N=4, NT=256, flags=gdn2._lib.SAVE_FOR_BWD,
+             dtype_qkv=gdn2._lib.BF16, dtype_bw=gdn2._lib.F32, scale=128 ** -0.5)
+    a.update(kw)
+    return gdn2._lib.ChunkArgs(**a)
+
+
+def test_workspace_sizes(gdn2):
+    lib = gdn2._lib.load()
+    ws = lib.gdn2_chunk_workspace_size(_args(gdn2))
+    tok = 4 * 4096 * 16
+    # G fp32 K, Aqk/A 64 bf16 each, Y/U/kg/qg bf16, v_new bf16, chunk states bf16
+    assert ws >= tok * (128 * 4 + 2 * 64 * 2 + 4 * 128 * 2 + 128 * 2) + 256 * 16 * 128 * 128 * 2
+    assert lib.gdn2_chunk_workspace_size(_args(gdn2, K=96)) == 0
+    assert lib.gdn2_chunk_bwd_workspace_size(_args(gdn2)) == 256 * 16 * 128 * 128 * 2 + tok * 128 * 2
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(K=96), 4), (dict(V=32), 4), (dict(dtype_qkv=1), 3), (dict(NT=255), 2),
+    (dict(N=3), 2), (dict(flags=4), 7),
+])
+def test_invalid_chunk_args_rejected(gdn2, kw, code):
+    lib = gdn2._lib.load()
+    st = lib.gdn2_chunk_fwd(_args(gdn2, **kw), None, 0, None)
+    assert st == code, gdn2._lib.load().gdn2_status_string(st)
+
+
+def test_null_pointers_and_workspace_rejected(gdn2):
+    lib = gdn2._lib.load()
+    assert lib.gdn2_chunk_fwd(_args(gdn2), None, 0, None) == 1  # q..o are NULL
+    buf = (ctypes.c_char * 64)()
+    p = ctypes.addressof(buf)
+    p16 = (p + 15) & ~15
+    a = _args(gdn2, q=p16, k=p16, v=p16, g=p16, b=p16, w=p16, o=p16)
+    assert lib.gdn2_chunk_fwd(a, None, 0, None) == 6  # workspace missing
+    a = _args(gdn2, q=p16 + 2, k=p16, v=p16, g=p16, b=p16, w=p16, o=p16)
+    assert lib.gdn2_chunk_fwd(a, None, 0, None) == 5  # misaligned
+
+
+def test_recurrent_args_rejected(gdn2):
+    lib = gdn2._lib.load()
+    R = gdn2._lib.RecurrentArgs
+    assert lib.gdn2_recurrent_fwd(R(B=2, T=1, H=3, HV=4, K=128, V=128, N=2), None) == 2  # HV % H
+    assert lib.gdn2_recurrent_fwd(R(B=2, T=1, H=2, HV=2, K=100, V=128, N=2), None) == 4
+    assert lib.gdn2_recurrent_fwd(R(B=2, T=1, H=2, HV=2, K=128, V=128, N=2), None) == 1
+
+
+def test_ops_fail_loudly_without_a_gpu(gdn2):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    x = torch.zeros(1, 64, 1, 64)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        gdn2.chunk_gdn2(x, x, x, x, x, x)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        gdn2.fused_recurrent_gdn2(x, x, x, x, x, x)
