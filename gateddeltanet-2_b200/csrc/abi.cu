@@ -53,6 +53,8 @@ const char* gdn2_status_string(int s) {
     case GDN2_ERR_WORKSPACE: return "workspace missing or too small";
     case GDN2_ERR_FLAGS: return "inconsistent flags";
     case GDN2_ERR_NO_DEVICE: return "no sm_100 device";
+    case GDN2_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the 32 MiB built-in scratch; use gdn2_chunk_fwd with a caller workspace";
     default: break;
   }
   if (s < 0) return cudaGetErrorString(static_cast<cudaError_t>(-s));

@@ -66,7 +66,8 @@ enum gdn2_status {
   GDN2_ERR_ALIGNMENT = 5,
   GDN2_ERR_WORKSPACE = 6,       /* workspace pointer NULL or too small */
   GDN2_ERR_FLAGS = 7,
-  GDN2_ERR_NO_DEVICE = 8
+  GDN2_ERR_NO_DEVICE = 8,
+  GDN2_ERR_SCRATCH_LIMIT = 9    /* problem larger than gdn2_chunk_fwd_static_scratch's 32 MiB */
 };
 
 /* ------------------------------------------------------------------------- */
@@ -132,6 +133,28 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* workspace, size_t workspace_b
 int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr,
                    const void* workspace, size_t workspace_bytes,
                    void* bwd_workspace, size_t bwd_workspace_bytes, gdn2_stream_t stream);
+
+/*
+ * Forward without any caller workspace, for callers that cannot allocate
+ * device memory (a serving engine that reserved the device up front and
+ * forbids later allocations, a plugin inside a framework that owns the
+ * allocator, a latency-critical loop that cannot afford an allocation's
+ * implicit synchronisation).  No counterpart in the reference: it has no C
+ * entry points, and its Python ops allocate through torch.
+ *
+ * Same arguments and results as gdn2_chunk_fwd without GDN2_SAVE_FOR_BWD
+ * (that flag is rejected: a backward needs a context that outlives the call).
+ * The scratch is one 32 MiB device array inside the library, present on every
+ * GPU that loads it until the process exits; problems whose
+ * gdn2_chunk_workspace_size exceeds 32 MiB return GDN2_ERR_SCRATCH_LIMIT (about
+ * 1.8 KB per token-head at K = V = 128: e.g. 16 heads x 1150 tokens fit).
+ * All calls share the array: calls whose kernels overlap on the GPU race, so
+ * serialise them.  Nothing in it needs clearing between calls.  The first call
+ * on each device resolves the array's device address (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.
+ * Nothing is allocated, by this call or by anything it calls.
+ */
+int gdn2_chunk_fwd_static_scratch(const gdn2_chunk_args* a, gdn2_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* token-serial recurrence (decode)                                          */
