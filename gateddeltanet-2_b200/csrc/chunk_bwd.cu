@@ -195,48 +195,69 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
 // ---------------------------------------------------------------------------
 // B3: chunk-parallel WY + intra backward
 // ---------------------------------------------------------------------------
-constexpr int kBIntraThreads = 256;
+// 16 warps: warp w owns rows [16 (w & 3), +16) and columns [(w >> 2) K/4, +K/4)
+// of every [64 x K] accumulator (dq, dk, db, dG), 16 fp32 registers each.
+constexpr int kBIntraThreads = 512;
+constexpr int kBIntraWarps = kBIntraThreads / 32;
 constexpr float kAnchorRangeB = 96.f;  // must match the forward's anchored range
 
-template <int K, int V>
+template <int K, int V, typename TB>
 struct BIntraSmem {
-  static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 8;
-  alignas(16) float G[kChunk][K];          // later reused for dG
+  // padded rows: accumulator-pattern accesses (8 rows x 4 column pairs per
+  // warp instruction) then fall in distinct banks
+  static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 8, LG = K + 4;
+  alignas(16) float G[kChunk][LG];         // later reused for dG
   alignas(16) __nv_bfloat16 A[kChunk][LA];
   alignas(16) __nv_bfloat16 DAqk[kChunk][LA];
   alignas(16) __nv_bfloat16 DT[kChunk][LA];
   alignas(16) float last[K];               // dgk_last + sum_r k dk_inter
-  alignas(16) float rsum[kChunk][2][2];    // l2norm row sums (q, k) per column half
+  alignas(16) float rsum[kChunk][4][2];    // l2norm row sums (q, k) per column group
   alignas(16) uint8_t flag[4][K];
   int nflag;
-  union alignas(128) {
-    struct {
-      alignas(16) __nv_bfloat16 DVN[kChunk][LV];
-      alignas(16) __nv_bfloat16 DY[kChunk][LK];
-      alignas(16) __nv_bfloat16 Hs[K][LV];
-      alignas(16) __nv_bfloat16 DH[K][LV];
-      alignas(16) __nv_bfloat16 DO[kChunk][LV];
-      alignas(16) __nv_bfloat16 VN[kChunk][LV];
-    } p1;
-    struct {
-      alignas(16) __nv_bfloat16 DVN[kChunk][LV];
-      alignas(16) __nv_bfloat16 DY[kChunk][LK];
-      alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
-      alignas(16) __nv_bfloat16 WV[kChunk][LV];
-      alignas(16) __nv_bfloat16 DA[kChunk][LA];
-      alignas(16) __nv_bfloat16 X[kChunk][LA];
-    } p2;
-    struct {
-      alignas(16) __nv_bfloat16 QG[kChunk][LK];
-      alignas(16) __nv_bfloat16 KBG[kChunk][LK];
-      alignas(16) __nv_bfloat16 KN[160][LK];
-    } p3;
-  } u;
+  // phase 1 needs h, dh, do, v_new, dv_new; phase 2 the WY operands; phase 3
+  // the anchored score operands.  q, k, b are staged once phase 1's products
+  // are done, in the part of the union phases 2 and 3 leave free.
+  struct P1 {
+    alignas(16) __nv_bfloat16 DVN[kChunk][LV];
+    alignas(16) __nv_bfloat16 DY[kChunk][LK];
+    alignas(16) __nv_bfloat16 Hs[K][LV];
+    alignas(16) __nv_bfloat16 DH[K][LV];
+    alignas(16) __nv_bfloat16 DO[kChunk][LV];
+    alignas(16) __nv_bfloat16 VN[kChunk][LV];
+  };
+  struct P2 {
+    alignas(16) __nv_bfloat16 DVN[kChunk][LV];
+    alignas(16) __nv_bfloat16 DY[kChunk][LK];
+    alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
+    alignas(16) __nv_bfloat16 WV[kChunk][LV];
+    alignas(16) __nv_bfloat16 DA[kChunk][LA];
+    alignas(16) __nv_bfloat16 X[kChunk][LA];
+  };
+  struct P3 {
+    alignas(16) __nv_bfloat16 QG[kChunk][LK];
+    alignas(16) __nv_bfloat16 KBG[kChunk][LK];
+    alignas(16) __nv_bfloat16 KN[160][LK];
+  };
+  static constexpr size_t kStageOff =
+      ((sizeof(P2) > sizeof(P3) ? sizeof(P2) : sizeof(P3)) + 127) / 128 * 128;
+  struct Staged {
+    alignas(16) __nv_bfloat16 Q[kChunk][LK];
+    alignas(16) __nv_bfloat16 Kk[kChunk][LK];
+    alignas(16) TB Bg[kChunk][K + 16 / sizeof(TB)];
+  };
+  static constexpr size_t kUnion =
+      sizeof(P1) > kStageOff + sizeof(Staged) ? sizeof(P1) : kStageOff + sizeof(Staged);
+  alignas(128) unsigned char u[kUnion];
+  GDN2_DEV P1& p1() { return *reinterpret_cast<P1*>(u); }
+  GDN2_DEV P2& p2() { return *reinterpret_cast<P2*>(u); }
+  GDN2_DEV P3& p3() { return *reinterpret_cast<P3*>(u); }
+  GDN2_DEV Staged& st() { return *reinterpret_cast<Staged*>(u + kStageOff); }
 };
 
-using BIntraSmem128x128 = BIntraSmem<128, 128>;
+using BIntraSmem128x128 = BIntraSmem<128, 128, float>;
 static_assert(offsetof(BIntraSmem128x128, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
-using BIntraSmem64x64 = BIntraSmem<64, 64>;
+static_assert(sizeof(BIntraSmem128x128) <= 227 * 1024, "B3 shared memory");
+using BIntraSmem64x64 = BIntraSmem<64, 64, float>;
 static_assert(offsetof(BIntraSmem64x64, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
 using BScanSmem128 = BScanSmem<128>;
 static_assert(offsetof(BScanSmem128, DSb) % 16 == 0 && sizeof(BScanStage<128>) % 16 == 0, "stage alignment");
@@ -250,8 +271,12 @@ template <int K, int V, typename TB>
 __global__ void __launch_bounds__(kBIntraThreads, 1)
 chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  using S = BIntraSmem<K, V>;
+  using S = BIntraSmem<K, V, TB>;
   S& sm = *reinterpret_cast<S*>(smem_raw);
+  auto& p1 = sm.p1();
+  auto& p2 = sm.p2();
+  auto& p3 = sm.p3();
+  auto& sg = sm.st();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t H = a.H, h = blockIdx.y, cglob = blockIdx.x;
   SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
@@ -263,15 +288,14 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   const int L = (int)(rem < kChunk ? rem : kChunk);
   const int64_t cidx = geo.chunk0(n) + ci;
   const float scale = a.scale;
-  const __nv_bfloat16* qn = ws.qn;
-  const __nv_bfloat16* kn = ws.kn;
   const __nv_bfloat16* vin = static_cast<const __nv_bfloat16*>(a.v);
   const __nv_bfloat16* dout = static_cast<const __nv_bfloat16*>(gr.dout);
   auto tokK = [&](int r, int c) { return ((t0 + r) * H + h) * K + c; };
   auto tokV = [&](int r, int c) { return ((t0 + r) * H + h) * V + c; };
-  auto qv = [&](int r, int c) { return r < L ? __bfloat162float(qn[tokK(r, c)]) : 0.f; };
-  auto kv = [&](int r, int c) { return r < L ? __bfloat162float(kn[tokK(r, c)]) : 0.f; };
-  auto bv = [&](int r, int c) { return r < L ? ldb<TB>(a.b, tokK(r, c)) : 0.f; };
+  // staged q, k, b (zero past the sequence end)
+  auto qv = [&](int r, int c) { return __bfloat162float(sg.Q[r][c]); };
+  auto kv = [&](int r, int c) { return __bfloat162float(sg.Kk[r][c]); };
+  auto bv = [&](int r, int c) { return to_f(sg.Bg[r][c]); };
 
   // ---- loads -----------------------------------------------------------------
   {
@@ -279,16 +303,16 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     const __nv_bfloat16* dhsrc = bw.dh + (cidx * H + h) * (int64_t)K * V;
     for (int i = tid; i < K * (V / 8); i += kBIntraThreads) {
       const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      cp_async16b(&sm.u.p1.Hs[r][p], hsrc + (int64_t)r * V + p, true);
-      cp_async16b(&sm.u.p1.DH[r][p], dhsrc + (int64_t)r * V + p, true);
+      cp_async16b(&p1.Hs[r][p], hsrc + (int64_t)r * V + p, true);
+      cp_async16b(&p1.DH[r][p], dhsrc + (int64_t)r * V + p, true);
     }
     for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
       const int r = i / (V / 8), p = (i % (V / 8)) * 8;
       const bool ok = r < L;
       const int64_t gi = tokV(ok ? r : 0, p);
-      cp_async16b(&sm.u.p1.DO[r][p], dout + gi, ok);
-      cp_async16b(&sm.u.p1.VN[r][p], ws.v_new + gi, ok);
-      cp_async16b(&sm.u.p1.DVN[r][p], bw.dvn + gi, ok);
+      cp_async16b(&p1.DO[r][p], dout + gi, ok);
+      cp_async16b(&p1.VN[r][p], ws.v_new + gi, ok);
+      cp_async16b(&p1.DVN[r][p], bw.dvn + gi, ok);
     }
     for (int i = tid; i < kChunk * (kChunk / 8); i += kBIntraThreads) {
       const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
@@ -317,8 +341,10 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 
   const int rb = warp & 3, ch = warp >> 2;
   const int m0 = rb * 16;
-  constexpr int NTk = K / 16, NTv = V / 16;
-  const int n0 = ch * (K / 2), n0v = ch * (V / 2);
+  constexpr int NTk = K / 32, NTv = V / 32;
+  const int n0 = ch * (K / 4), n0v = ch * (V / 4);
+  // 64x64 products: warp tile 16 x 16
+  const int mm = (warp & 3) * 16, nn = (warp >> 2) * 16;
   float dq[1][NTk][4], dk[1][NTk][4], db[1][NTk][4], dG[1][NTk][4];
   zero_acc(dq);
   zero_acc(dk);
@@ -327,17 +353,81 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   const float* Glast = &sm.G[kChunk - 1][0];
 
   // ---- phase 1: products with h, dh ------------------------------------------
-  warp_mma<1, NTk, false, true>(dq, Smem{&sm.u.p1.DO[0][0], S::LV}, m0, Smem{&sm.u.p1.Hs[0][0], S::LV}, n0, 0, V,
-                                lane);
-  warp_mma<1, NTk, false, true>(dk, Smem{&sm.u.p1.VN[0][0], S::LV}, m0, Smem{&sm.u.p1.DH[0][0], S::LV}, n0, 0, V,
-                                lane);
+  warp_mma<1, NTk, false, true>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.Hs[0][0], S::LV}, n0, 0, V, lane);
+  warp_mma<1, NTk, false, true>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DH[0][0], S::LV}, n0, 0, V, lane);
   {
     float t[1][NTk][4];
     zero_acc(t);
-    warp_mma<1, NTk, false, true>(t, Smem{&sm.u.p1.DVN[0][0], S::LV}, m0, Smem{&sm.u.p1.Hs[0][0], S::LV}, n0, 0, V,
-                                  lane);
-    acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { sm.u.p1.DY[r][c] = __float2bfloat16_rn(-v); });
+    warp_mma<1, NTk, false, true>(t, Smem{&p1.DVN[0][0], S::LV}, m0, Smem{&p1.Hs[0][0], S::LV}, n0, 0, V, lane);
+    acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { p1.DY[r][c] = __float2bfloat16_rn(-v); });
   }
+  // dgk_last = 2^G_last * sum_v h dh  (4 threads per state row)
+  {
+    const int r = tid >> 2, part = tid & 3;
+    float s = 0.f;
+    if (r < K) {
+      for (int v = part * (V / 4); v < (part + 1) * (V / 4); ++v)
+        s += __bfloat162float(p1.Hs[r][v]) * __bfloat162float(p1.DH[r][v]);
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (r < K && part == 0) atomicAdd(&sm.last[r], s * exp2_approx(Glast[r]));
+  }
+  // dAqk = scale do v_new^T (lower incl. diagonal)
+  {
+    float t[1][2][4];
+    zero_acc(t);
+    warp_mma<1, 2, false, true>(t, Smem{&p1.DO[0][0], S::LV}, mm, Smem{&p1.VN[0][0], S::LV}, nn, 0, V, lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+      sm.DAqk[r][s] = __float2bfloat16_rn((s <= r && r < L) ? v * scale : 0.f);
+    });
+  }
+  __syncthreads();  // h, dh, do, v_new are dead: stage q, k, b in their place
+  for (int i = tid; i < kChunk * (K / 8); i += kBIntraThreads) {
+    const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+    const bool ok = r < L;
+    const int64_t gi = tokK(ok ? r : 0, p);
+    cp_async16b(&sg.Q[r][p], ws.qn + gi, ok);
+    cp_async16b(&sg.Kk[r][p], ws.kn + gi, ok);
+  }
+  constexpr int kBPer16 = 16 / sizeof(TB);
+  for (int i = tid; i < kChunk * (K / kBPer16); i += kBIntraThreads) {
+    const int r = i / (K / kBPer16), p = (i % (K / kBPer16)) * kBPer16;
+    const bool ok = r < L;
+    cp_async16b(&sg.Bg[r][p], static_cast<const TB*>(a.b) + tokK(ok ? r : 0, p), ok);
+  }
+  cp_commit();
+  // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv)   (overlaps the staging)
+  {
+    float t[1][NTv][4];
+    zero_acc(t);
+    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
+                                  lane);
+    __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
+    TB* dw = static_cast<TB*>(gr.dw);
+    float wl[NTv][4], vl[NTv][4];
+#pragma unroll
+    for (int j = 0; j < NTv; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0v + 8 * j + 2 * (lane & 3) + (e & 1);
+        wl[j][e] = r < L ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
+        vl[j][e] = r < L ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
+      }
+#pragma unroll
+    for (int j = 0; j < NTv; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0v + 8 * j + 2 * (lane & 3) + (e & 1);
+        if (r < L) {
+          const int64_t gi = tokV(r, c);
+          dv[gi] = __float2bfloat16_rn(t[0][j][e] * wl[j][e]);
+          dw[gi] = from_f<TB>(t[0][j][e] * vl[j][e]);
+        }
+      }
+  }
+  cp_wait<0>();
+  __syncthreads();
   // inter-chunk parts: dq = scale (do h^T) 2^G ; dk = (v_new dh^T) 2^(G_last - G)
   {
     float colsum[NTk][2];
@@ -357,7 +447,6 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         dG[0][j][e] = qv(r, c) * dqi - kk * dki;
         colsum[j][e & 1] += kk * dki;
       }
-    // sum over the warp's 16 rows (lanes sharing lane&3), then across row blocks
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
@@ -369,102 +458,48 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         if (lane < 4) atomicAdd(&sm.last[n0 + 8 * j + 2 * lane + x], s);
       }
   }
-  // dgk_last = 2^G_last * sum_v h dh  (2 threads per state row)
-  {
-    const int r = tid >> 1, half = tid & 1;
-    float s = 0.f;
-    if (r < K) {
-      for (int v = half * (V / 2); v < (half + 1) * (V / 2); ++v)
-        s += __bfloat162float(sm.u.p1.Hs[r][v]) * __bfloat162float(sm.u.p1.DH[r][v]);
-    }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (r < K && half == 0) atomicAdd(&sm.last[r], s * exp2_approx(Glast[r]));
-  }
-  // dAqk = scale do v_new^T (lower incl. diagonal)
-  {
-    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
-    float t[1][4][4];
-    zero_acc(t);
-    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p1.DO[0][0], S::LV}, mm, Smem{&sm.u.p1.VN[0][0], S::LV}, nn, 0, V,
-                                lane);
-    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
-      sm.DAqk[r][s] = __float2bfloat16_rn((s <= r && r < L) ? v * scale : 0.f);
-    });
-  }
-  // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv)
-  {
-    float t[1][NTv][4];
-    zero_acc(t);
-    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&sm.u.p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
-                                  lane);
-    __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
-    TB* dw = static_cast<TB*>(gr.dw);
-    acc_foreach(t, m0, n0v, lane, [&](float v, int r, int c) {
-      if (r < L) {
-        const int64_t gi = tokV(r, c);
-        dv[gi] = __float2bfloat16_rn(v * ldb<TB>(a.w, gi));
-        dw[gi] = from_f<TB>(v * __bfloat162float(vin[gi]));
-      }
-    });
-  }
-  __syncthreads();
 
   // ---- phase 2: WY factors -----------------------------------------------------
-  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kBIntraThreads) {
-    float b8[8], k8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
-      b8[u] = bv(r, c);
-      k8[u] = kv(r, c);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
-      sm.u.p2.KB2G[r][c] = __float2bfloat16_rn(b8[u] * k8[u] * exp2_approx(sm.G[r][c]));
-    }
+  for (int i = tid; i < kChunk * K; i += kBIntraThreads) {
+    const int r = i / K, c = i % K;
+    p2.KB2G[r][c] = __float2bfloat16_rn(bv(r, c) * kv(r, c) * exp2_approx(sm.G[r][c]));
   }
   for (int i0 = tid; i0 < kChunk * V; i0 += 8 * kBIntraThreads) {
     float w8[8], v8[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
-      w8[u] = r < L ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
-      v8[u] = r < L ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
+      w8[u] = (i < kChunk * V && r < L) ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
+      v8[u] = (i < kChunk * V && r < L) ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
-      sm.u.p2.WV[r][c] = __float2bfloat16_rn(w8[u] * v8[u]);
+      if (i < kChunk * V) p2.WV[r][c] = __float2bfloat16_rn(w8[u] * v8[u]);
     }
   }
   __syncthreads();
   {
-    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
-    float t[1][4][4];
+    float t[1][2][4];
     zero_acc(t);
-    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DVN[0][0], S::LV}, mm, Smem{&sm.u.p2.WV[0][0], S::LV}, nn, 0, V,
-                                lane);
-    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DY[0][0], S::LK}, mm, Smem{&sm.u.p2.KB2G[0][0], S::LK}, nn, 0, K,
-                                lane);
+    warp_mma<1, 2, false, true>(t, Smem{&p2.DVN[0][0], S::LV}, mm, Smem{&p2.WV[0][0], S::LV}, nn, 0, V, lane);
+    warp_mma<1, 2, false, true>(t, Smem{&p2.DY[0][0], S::LK}, mm, Smem{&p2.KB2G[0][0], S::LK}, nn, 0, K, lane);
     acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
-      sm.u.p2.DA[r][s] = __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
+      p2.DA[r][s] = __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
     });
   }
   // d(b k 2^G) = A^T dY
   {
     float t[1][NTk][4];
     zero_acc(t);
-    warp_mma<1, NTk, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&sm.u.p2.DY[0][0], S::LK}, n0, 0, kChunk,
-                                  lane);
+    warp_mma<1, NTk, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p2.DY[0][0], S::LK}, n0, 0, kChunk, lane);
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
         if (r < L) {
-          const float ex = exp2_approx(sm.G[r][c]);
-          const float x = t[0][j][e] * ex;
+          const float x = t[0][j][e] * exp2_approx(sm.G[r][c]);
           const float bb = bv(r, c), kk = kv(r, c);
           db[0][j][e] += kk * x;
           dk[0][j][e] += bb * x;
@@ -475,14 +510,13 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   __syncthreads();
   // dT = -A^T (dA A^T), strictly lower
   {
-    const int mm = (warp & 3) * 16, nn = (warp >> 2) * 32;
-    float t[1][4][4];
+    float t[1][2][4];
     zero_acc(t);
-    warp_mma<1, 4, false, true>(t, Smem{&sm.u.p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
-    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) { sm.u.p2.X[r][s] = __float2bfloat16_rn(v); });
+    warp_mma<1, 2, false, true>(t, Smem{&p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
+    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) { p2.X[r][s] = __float2bfloat16_rn(v); });
     __syncthreads();
     zero_acc(t);
-    warp_mma<1, 4, true, false>(t, Smem{&sm.A[0][0], S::LA}, mm, Smem{&sm.u.p2.X[0][0], S::LA}, nn, 0, kChunk, lane);
+    warp_mma<1, 2, true, false>(t, Smem{&sm.A[0][0], S::LA}, mm, Smem{&p2.X[0][0], S::LA}, nn, 0, kChunk, lane);
     acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
       sm.DT[r][s] = __float2bfloat16_rn((s < r && r < L) ? -v : 0.f);
     });
@@ -490,31 +524,20 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   __syncthreads();
 
   // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
-  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kBIntraThreads) {
-    float q8[8], k8[8], b8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
-      q8[u] = qv(r, c);
-      k8[u] = kv(r, c);
-      b8[u] = bv(r, c);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / K, c = i % K;
-      const int blk = r >> 4, a0 = blk * 16;
-      const float kk = k8[u];
-      const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);
-      sm.u.p3.QG[r][c] = __float2bfloat16_rn(q8[u] * rowf);
-      sm.u.p3.KBG[r][c] = __float2bfloat16_rn(b8[u] * kk * rowf);
-      const float fd = sm.flag[blk][c] ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);
-      sm.u.p3.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kk * fd);
-      if (blk < 3) {
-        float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);
-        for (int ai = blk + 1; ai < 4; ++ai) {
-          if (ai > blk + 1) f *= exp2_approx(sm.G[ai * 16][c] - sm.G[ai * 16 - 16][c]);
-          sm.u.p3.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kk * f);
-        }
+  for (int i = tid; i < kChunk * K; i += kBIntraThreads) {
+    const int r = i / K, c = i % K;
+    const int blk = r >> 4, a0 = blk * 16;
+    const float kk = kv(r, c);
+    const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);
+    p3.QG[r][c] = __float2bfloat16_rn(qv(r, c) * rowf);
+    p3.KBG[r][c] = __float2bfloat16_rn(bv(r, c) * kk * rowf);
+    const float fd = sm.flag[blk][c] ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);
+    p3.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kk * fd);
+    if (blk < 3) {
+      float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);
+      for (int ai = blk + 1; ai < 4; ++ai) {
+        if (ai > blk + 1) f *= exp2_approx(sm.G[ai * 16][c] - sm.G[ai * 16 - 16][c]);
+        p3.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kk * f);
       }
     }
   }
@@ -524,7 +547,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     float r1[1][NTk][4], r2[1][NTk][4];
     zero_acc(r1);
     zero_acc(r2);
-    Smem KNi{&sm.u.p3.KN[anchor_row0(rb)][0], S::LK};
+    Smem KNi{&p3.KN[anchor_row0(rb)][0], S::LK};
     warp_mma<1, NTk, false, false>(r1, Smem{&sm.DAqk[0][0], S::LA}, m0, KNi, n0, 0, 16 * (rb + 1), lane);
     warp_mma<1, NTk, false, false>(r2, Smem{&sm.DT[0][0], S::LA}, m0, KNi, n0, 0, 16 * (rb + 1), lane);
 #pragma unroll
@@ -533,40 +556,36 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       for (int e = 0; e < 4; ++e) {
         const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
         const float rowf = exp2_approx(sm.G[r][c] - sm.G[m0][c]);
-        const float dqi = r1[0][j][e] * rowf;
         const float rr = r2[0][j][e] * rowf;
-        const float kk = kv(r, c), bb = bv(r, c);
-        dq[0][j][e] += dqi;
-        dk[0][j][e] += rr * bb;
-        db[0][j][e] += rr * kk;
+        dq[0][j][e] += r1[0][j][e] * rowf;
+        dk[0][j][e] += rr * bv(r, c);
+        db[0][j][e] += rr * kv(r, c);
         // the decay-gradient pieces use the very bf16 operands the MMAs read
         // (QG = q 2^(G_r - G_a), KBG = b k 2^(G_r - G_a)), so that the row and
         // column sides below cancel exactly when summed over the chunk.
-        dG[0][j][e] += __bfloat162float(sm.u.p3.QG[r][c]) * r1[0][j][e] +
-                       __bfloat162float(sm.u.p3.KBG[r][c]) * r2[0][j][e];
+        dG[0][j][e] += __bfloat162float(p3.QG[r][c]) * r1[0][j][e] +
+                       __bfloat162float(p3.KBG[r][c]) * r2[0][j][e];
       }
   }
-  {
-    // column parts: this warp's rows as columns s of block rb, rows r of blocks >= rb
-    for (int ib = rb; ib < 4; ++ib) {
-      float cc[1][NTk][4];
-      zero_acc(cc);
-      warp_mma<1, NTk, true, false>(cc, Smem{&sm.DAqk[0][0], S::LA}, m0, Smem{&sm.u.p3.QG[0][0], S::LK}, n0, ib * 16,
-                                    ib * 16 + 16, lane);
-      warp_mma<1, NTk, true, false>(cc, Smem{&sm.DT[0][0], S::LA}, m0, Smem{&sm.u.p3.KBG[0][0], S::LK}, n0, ib * 16,
-                                    ib * 16 + 16, lane);
+  // column parts: this warp's rows as columns s of block rb, rows r of blocks >= rb
+  for (int ib = rb; ib < 4; ++ib) {
+    float cc[1][NTk][4];
+    zero_acc(cc);
+    warp_mma<1, NTk, true, false>(cc, Smem{&sm.DAqk[0][0], S::LA}, m0, Smem{&p3.QG[0][0], S::LK}, n0, ib * 16,
+                                  ib * 16 + 16, lane);
+    warp_mma<1, NTk, true, false>(cc, Smem{&sm.DT[0][0], S::LA}, m0, Smem{&p3.KBG[0][0], S::LK}, n0, ib * 16,
+                                  ib * 16 + 16, lane);
 #pragma unroll
-      for (int j = 0; j < NTk; ++j)
+    for (int j = 0; j < NTk; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int s = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-          float cf = exp2_approx(sm.G[ib * 16][c] - sm.G[s][c]);
-          if (ib == rb && sm.flag[rb][c]) cf = 0.f;
-          dk[0][j][e] += cc[0][j][e] * cf;
-          // KN_ib[s] = bf16(k_s 2^(G_a - G_s)): the row side's operand
-          dG[0][j][e] -= __bfloat162float(sm.u.p3.KN[anchor_row0(ib) + s][c]) * cc[0][j][e];
-        }
-    }
+      for (int e = 0; e < 4; ++e) {
+        const int s = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+        float cf = exp2_approx(sm.G[ib * 16][c] - sm.G[s][c]);
+        if (ib == rb && sm.flag[rb][c]) cf = 0.f;
+        dk[0][j][e] += cc[0][j][e] * cf;
+        // KN_ib[s] = bf16(k_s 2^(G_a - G_s)): the row side's operand
+        dG[0][j][e] -= __bfloat162float(p3.KN[anchor_row0(ib) + s][c]) * cc[0][j][e];
+      }
   }
   // exact per-pair contributions of flagged (block, channel)s
   if (sm.nflag > 0) {
@@ -644,8 +663,12 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         const int64_t gi = tokK(r, c);
         float xq = dq[0][j][e], xk = dk[0][j][e];
         if (l2) {
-          const float sq = sm.rsum[r][0][0] + sm.rsum[r][1][0];
-          const float sk = sm.rsum[r][0][1] + sm.rsum[r][1][1];
+          float sq = 0.f, sk = 0.f;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            sq += sm.rsum[r][x][0];
+            sk += sm.rsum[r][x][1];
+          }
           const float rq = ws.q_rstd[(t0 + r) * H + h], rk = ws.k_rstd[(t0 + r) * H + h];
           xq = (xq - sq * qv(r, c)) * rq;
           xk = (xk - sk * kv(r, c)) * rk;
@@ -669,8 +692,8 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       if (gate) {
         const float x = a.g[gi] + bias;
         if (lbnd) {
-          const float sg = sigmoid_f(Aexp * x);
-          out = acc * a.lower_bound * sg * (1.f - sg) * Aexp;
+          const float s2 = sigmoid_f(Aexp * x);
+          out = acc * a.lower_bound * s2 * (1.f - s2) * Aexp;
           dA += out * x;
         } else {
           out = -Aexp * acc * sigmoid_f(x);
@@ -703,9 +726,9 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
   }
   GDN2_LAUNCH_CHECK();
   if (a.NT > 0) {
-    const size_t sm3 = sizeof(BIntraSmem<K, V>);
-    auto k3 = a.dtype_bw == GDN2_BF16 ? chunk_bwd_intra_kernel<K, V, __nv_bfloat16>
-                                      : chunk_bwd_intra_kernel<K, V, float>;
+    const bool bwb = a.dtype_bw == GDN2_BF16;
+    const size_t sm3 = bwb ? sizeof(BIntraSmem<K, V, __nv_bfloat16>) : sizeof(BIntraSmem<K, V, float>);
+    auto k3 = bwb ? chunk_bwd_intra_kernel<K, V, __nv_bfloat16> : chunk_bwd_intra_kernel<K, V, float>;
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3));
     dim3 g3((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKBwdIntra, s);

@@ -68,9 +68,9 @@ struct IntraSmem {
     } s;
     struct {
       alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
-      alignas(16) __nv_bfloat16 WV[kChunk][LV];
     } w;
   } u;
+  alignas(16) __nv_bfloat16 WV[kChunk][LV];  // w * v, formed right after the loads
   alignas(16) float P[4][16][17];        // solve scratch
   alignas(16) float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
   alignas(16) uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
@@ -81,6 +81,10 @@ using IntraSmem128x128 = IntraSmem<128, 128>;
 static_assert(offsetof(IntraSmem128x128, u) % 128 == 0, "ldmatrix targets need 16B alignment");
 using IntraSmem64x64 = IntraSmem<64, 64>;
 static_assert(offsetof(IntraSmem64x64, u) % 128 == 0, "ldmatrix targets need 16B alignment");
+static_assert(sizeof(IntraSmem128x128) <= 227 * 1024, "F1 shared memory");
+// w (fp32) and v (bf16) are parked in Aqk/Tm and Af while those are unused
+static_assert(2 * sizeof(float) * kChunk * (kChunk + 4) >= sizeof(float) * kChunk * 128, "w staging");
+static_assert(sizeof(float) * kChunk * (kChunk + 4) >= 2 * kChunk * 128, "v staging");
 
 template <typename TB>
 GDN2_DEV float ld_bw(const void* p, int64_t i) {
@@ -122,9 +126,41 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     const bool ok = r < L;
     cp_async16(&sm.G[r][p], a.g + ((t0 + (ok ? r : 0)) * H + h) * K + p, ok);
   }
+  // w (TB) and v (bf16) ride along, parked in the score buffers (free until step 4)
+  {
+    TB* wst = reinterpret_cast<TB*>(&sm.Aqk[0][0]);            // [64][V] TB, fits Aqk+Tm
+    __nv_bfloat16* vst = reinterpret_cast<__nv_bfloat16*>(&sm.Af[0][0]);  // [64][V] bf16
+    constexpr int kWPer16 = 16 / sizeof(TB);
+    for (int i = tid; i < kChunk * (V / kWPer16); i += kIntraThreads) {
+      const int r = i / (V / kWPer16), p = (i % (V / kWPer16)) * kWPer16;
+      const bool ok = r < L;
+      cp_async16(wst + r * V + p, static_cast<const TB*>(a.w) + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
+    }
+    for (int i = tid; i < kChunk * (V / 8); i += kIntraThreads) {
+      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+      const bool ok = r < L;
+      cp_async16(vst + r * V + p, vin + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
+    }
+  }
   cp_async_commit();
+  // each thread's b values for steps 3 and 7 (element i = tid + 256 u), issued now
+  constexpr int kBPerThread = kChunk * K / kIntraThreads;
+  float breg[kBPerThread];
+#pragma unroll
+  for (int u = 0; u < kBPerThread; ++u) {
+    const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
+    breg[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
+  }
   cp_async_wait<0>();
   __syncthreads();
+  {
+    const TB* wst = reinterpret_cast<const TB*>(&sm.Aqk[0][0]);
+    const __nv_bfloat16* vst = reinterpret_cast<const __nv_bfloat16*>(&sm.Af[0][0]);
+    for (int i = tid; i < kChunk * V; i += kIntraThreads) {
+      const int r = i / V, c = i % V;
+      sm.WV[r][c] = __float2bfloat16_rn(to_f(wst[r * V + c]) * __bfloat162float(vst[r * V + c]));
+    }
+  }
   if (l2) {
     // warp w owns rows 8w..8w+7; lane owns channels lane, lane+32, ...
     for (int rr = 0; rr < 8; ++rr) {
@@ -202,20 +238,14 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   for (int i = tid; i < 4 * K; i += kIntraThreads) {
     if (sm.flag[i / K][i % K]) atomicAdd(&sm.nflag[i / K], 1);
   }
-  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kIntraThreads) {
-    float bv8[8];
+  {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
-      bv8[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+    for (int u = 0; u < kBPerThread; ++u) {
+      const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
       const int blk = r >> 4, a0 = blk * 16;
       const float kq = __bfloat162float(sm.Kt[r][c]);
       const float qq = __bfloat162float(sm.Q[r][c]);
-      const float bb = bv8[u];
+      const float bb = breg[u];
       const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);  // <= 1
       sm.u.s.QG[r][c] = __float2bfloat16_rn(qq * rowf);
       sm.u.s.KBG[r][c] = __float2bfloat16_rn(bb * kq * rowf);
@@ -350,41 +380,20 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   }
   // WY operands (the score operands are dead now)
   __syncthreads();
-  for (int i0 = tid; i0 < kChunk * K; i0 += 8 * kIntraThreads) {
-    float bv8[8];
+  {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
-      bv8[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / K, c = i % K;
+    for (int u = 0; u < kBPerThread; ++u) {
+      const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
       const float kq = __bfloat162float(sm.Kt[r][c]);
       const float qq = __bfloat162float(sm.Q[r][c]);
       const float Gr = sm.G[r][c];
       const float e = exp2_approx(Gr);
-      sm.u.w.KB2G[r][c] = __float2bfloat16_rn(bv8[u] * kq * e);
+      sm.u.w.KB2G[r][c] = __float2bfloat16_rn(breg[u] * kq * e);
       if (r < L) {
         const int64_t gi = ((t0 + r) * H + h) * K + c;
         ws.kg[gi] = __float2bfloat16_rn(kq * exp2_approx(sm.G[kChunk - 1][c] - Gr));
         ws.qg[gi] = __float2bfloat16_rn(qq * e);
       }
-    }
-  }
-  for (int i0 = tid; i0 < kChunk * V; i0 += 8 * kIntraThreads) {
-    float wv8[8], vv8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / V, c = i % V;
-      const int64_t gi = ((t0 + r) * H + h) * V + c;
-      wv8[u] = r < L ? ld_bw<TB>(a.w, gi) : 0.f;
-      vv8[u] = r < L ? __bfloat162float(vin[gi]) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kIntraThreads, r = i / V, c = i % V;
-      sm.u.w.WV[r][c] = __float2bfloat16_rn(wv8[u] * vv8[u]);
     }
   }
   __syncthreads();
@@ -409,7 +418,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       const int n0 = (warp >> 2) * (V / 2);
       float acc[1][NTc][4];
       zero_acc(acc);
-      warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.u.w.WV[0][0], S::LV}, n0, 0, kChunk, lane);
+      warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.WV[0][0], S::LV}, n0, 0, kChunk, lane);
       acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
         if (r < L) ws.U[((t0 + r) * H + h) * V + c] = __float2bfloat16_rn(v);
       });
