@@ -133,34 +133,35 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
     const int64_t t0 = bos + ci * kChunk;
     const int L = chunk_len(ci);
     BScanStage<K>& st = sm.st[ci & 1];
-    if (sown) {
-      acc_foreach(dS, sr0, 0, lane, [&](float& v, int r, int c) {
-        const __nv_bfloat16 b = __float2bfloat16_rn(v);
-        sm.DSb[r][c] = b;
-        bw.dh[((c0 + ci) * H + h) * (int64_t)K * V + (int64_t)r * V + v0 + c] = b;
-      });
-    }
+    if (sown) acc_foreach(dS, sr0, 0, lane, [&](float& v, int r, int c) { sm.DSb[r][c] = __float2bfloat16_rn(v); });
     if (ci > 0) bscan_prefetch<K, V>(sm.st[(ci - 1) & 1], ws, dout, a, t0 - kChunk, chunk_len(ci - 1), h, v0, tid);
     cp_commit();
     cp_wait<1>();
     __syncthreads();
+    {  // dh of this chunk, 16-byte stores out of DSb
+      __nv_bfloat16* dst = bw.dh + ((c0 + ci) * H + h) * (int64_t)K * V + v0;
+      for (int i = tid; i < K * (kBScanBV / 8); i += kBScanThreads) {
+        const int r = i / (kBScanBV / 8), p = (i % (kBScanBV / 8)) * 8;
+        *reinterpret_cast<uint4*>(dst + (int64_t)r * V + p) = *reinterpret_cast<const uint4*>(&sm.DSb[r][p]);
+      }
+    }
 
     // dv_new = Aqk^T do + kg dS      (warp tile 16 x 32)
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
     {
       float acc[1][4][4];
       zero_acc(acc);
-      warp_mma<1, 4, true, false>(acc, Smem{&st.Aqk[0][0], BScanStage<K>::LA}, m0,
-                                  Smem{&st.DO[0][0], BScanStage<K>::LV}, n0, 0, kChunk, lane);
-      warp_mma<1, 4, false, false>(acc, Smem{&st.KG[0][0], BScanStage<K>::LK}, m0,
-                                   Smem{&sm.DSb[0][0], kBScanBV + 8}, n0, 0, K, lane);
-      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
-        const __nv_bfloat16 b = __float2bfloat16_rn(r < L ? v : 0.f);
-        sm.DV[r][c] = b;
-        if (r < L) bw.dvn[((t0 + r) * H + h) * V + v0 + c] = b;
-      });
+      warp_mma_ks<2, 1, 4, true, false>(acc, Smem{&st.Aqk[0][0], BScanStage<K>::LA}, m0,
+                                        Smem{&st.DO[0][0], BScanStage<K>::LV}, n0, 0, kChunk, lane);
+      warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.KG[0][0], BScanStage<K>::LK}, m0,
+                                         Smem{&sm.DSb[0][0], kBScanBV + 8}, n0, 0, K, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) { sm.DV[r][c] = __float2bfloat16_rn(r < L ? v : 0.f); });
     }
     __syncthreads();
+    for (int i = tid; i < L * (kBScanBV / 8); i += kBScanThreads) {
+      const int r = i / (kBScanBV / 8), p = (i % (kBScanBV / 8)) * 8;
+      *reinterpret_cast<uint4*>(bw.dvn + ((t0 + r) * H + h) * V + v0 + p) = *reinterpret_cast<const uint4*>(&sm.DV[r][p]);
+    }
     // dS <- 2^G_last dS + scale qg^T do - Y^T dv_new
     if (sown) {
       float t1[MT][NT][4], t2[MT][NT][4];
@@ -170,15 +171,18 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
                                     Smem{&st.DO[0][0], BScanStage<K>::LV}, 0, 0, kChunk, lane);
       warp_mma<MT, NT, true, false>(t2, Smem{&st.Y[0][0], BScanStage<K>::LK}, sr0,
                                     Smem{&sm.DV[0][0], kBScanBV + 8}, 0, 0, kChunk, lane);
+      float dec[MT][2];
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) dec[i][x] = exp2_approx(st.glast[sr0 + 16 * i + (lane >> 2) + 8 * x]);
 #pragma unroll
       for (int i = 0; i < MT; ++i)
 #pragma unroll
         for (int j = 0; j < NT; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int r = sr0 + 16 * i + (lane >> 2) + (e >> 1) * 8;
-            dS[i][j][e] = dS[i][j][e] * exp2_approx(st.glast[r]) + a.scale * t1[i][j][e] - t2[i][j][e];
-          }
+          for (int e = 0; e < 4; ++e)
+            dS[i][j][e] = dS[i][j][e] * dec[i][e >> 1] + a.scale * t1[i][j][e] - t2[i][j][e];
     }
     __syncthreads();
   }

@@ -448,6 +448,7 @@ struct ScanSmem {
   ScanStage<K> st[2];
   alignas(16) __nv_bfloat16 Sb[K][kScanBV + 8];      // bf16 copy of the state (MMA operand)
   alignas(16) __nv_bfloat16 VN[kChunk][kScanBV + 8]; // v_new (bf16)
+  alignas(16) __nv_bfloat16 O[kChunk][kScanBV + 8];  // output tile, written out with 16-byte stores
 };
 
 template <int K, int V>
@@ -523,17 +524,8 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
     const int64_t t0 = bos + ci * kChunk;
     const int L = (int)(kChunk < (len - ci * kChunk) ? (int64_t)kChunk : (len - ci * kChunk));
     ScanStage<K>& st = sm.st[ci & 1];
-    // state -> bf16 operand (and the saved per-chunk state h)
-    if (sown) {
-      acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
-        const __nv_bfloat16 b = __float2bfloat16_rn(v);
-        sm.Sb[r][c] = b;
-        if (save) {
-          __nv_bfloat16* hdst = ws.h + ((c0 + ci) * H + h) * (int64_t)K * V;
-          hdst[(int64_t)r * V + v0 + c] = b;
-        }
-      });
-    }
+    // state -> bf16 operand
+    if (sown) acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) { sm.Sb[r][c] = __float2bfloat16_rn(v); });
     if (ci + 1 < nchunks) {
       const int Ln = (int)(kChunk < (len - (ci + 1) * kChunk) ? (int64_t)kChunk : (len - (ci + 1) * kChunk));
       scan_prefetch<K, V>(sm.st[(ci + 1) & 1], ws, a, t0 + kChunk, Ln, h, v0, tid);
@@ -541,42 +533,65 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
+    if (save) {  // the chunk's entering state h, 16-byte stores out of Sb
+      __nv_bfloat16* hdst = ws.h + ((c0 + ci) * H + h) * (int64_t)K * V + v0;
+      for (int i = tid; i < K * (kScanBV / 8); i += kScanThreads) {
+        const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
+        *reinterpret_cast<uint4*>(hdst + (int64_t)r * V + p) = *reinterpret_cast<const uint4*>(&sm.Sb[r][p]);
+      }
+    }
 
     // v_new = U - Y S : warp tile 16 rows x 32 cols (8 warps cover 64 x 64)
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
     {
       float acc[1][4][4];
       zero_acc(acc);
-      warp_mma<1, 4, false, false>(acc, Smem{&st.Y[0][0], ScanStage<K>::LK}, m0, Smem{&sm.Sb[0][0], kScanBV + 8},
-                                   n0, 0, K, lane);
+      warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.Y[0][0], ScanStage<K>::LK}, m0,
+                                         Smem{&sm.Sb[0][0], kScanBV + 8}, n0, 0, K, lane);
       acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
-        const float vn = r < L ? __bfloat162float(st.U[r][c]) - v : 0.f;
-        const __nv_bfloat16 b = __float2bfloat16_rn(vn);
-        sm.VN[r][c] = b;
-        if (save && r < L) ws.v_new[((t0 + r) * H + h) * V + v0 + c] = b;
+        sm.VN[r][c] = __float2bfloat16_rn(r < L ? __bfloat162float(st.U[r][c]) - v : 0.f);
       });
     }
     __syncthreads();
+    if (save) {
+      for (int i = tid; i < L * (kScanBV / 8); i += kScanThreads) {
+        const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
+        *reinterpret_cast<uint4*>(ws.v_new + ((t0 + r) * H + h) * V + v0 + p) =
+            *reinterpret_cast<const uint4*>(&sm.VN[r][p]);
+      }
+    }
     // o = scale * qg S + Aqk v_new
     {
       float acc[1][4][4];
       zero_acc(acc);
-      warp_mma<1, 4, false, false>(acc, Smem{&st.QG[0][0], ScanStage<K>::LK}, m0, Smem{&sm.Sb[0][0], kScanBV + 8},
-                                   n0, 0, K, lane);
+      warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.QG[0][0], ScanStage<K>::LK}, m0,
+                                         Smem{&sm.Sb[0][0], kScanBV + 8}, n0, 0, K, lane);
       acc_foreach(acc, m0, n0, lane, [&](float& v, int, int) { v *= a.scale; });
-      warp_mma<1, 4, false, false>(acc, Smem{&st.Aqk[0][0], ScanStage<K>::LA}, m0,
-                                   Smem{&sm.VN[0][0], kScanBV + 8}, n0, 0, kChunk, lane);
-      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
-        if (r < L) o[((t0 + r) * H + h) * V + v0 + c] = __float2bfloat16_rn(v);
-      });
+      warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.Aqk[0][0], ScanStage<K>::LA}, m0,
+                                         Smem{&sm.VN[0][0], kScanBV + 8}, n0, 0, kChunk, lane);
+      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) { sm.O[r][c] = __float2bfloat16_rn(v); });
     }
     // S <- 2^G_last S + kg^T v_new
     if (sown) {
-      acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int) { v *= exp2_approx(st.glast[r]); });
+      float dec[MT][2];
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int x = 0; x < 2; ++x) dec[i][x] = exp2_approx(st.glast[sr0 + 16 * i + (lane >> 2) + 8 * x]);
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) S[i][j][e] *= dec[i][e >> 1];
       warp_mma<MT, NT, true, false>(S, Smem{&st.KG[0][0], ScanStage<K>::LK}, sr0, Smem{&sm.VN[0][0], kScanBV + 8},
                                     0, 0, kChunk, lane);
     }
-    __syncthreads();  // stage buffers and Sb are rewritten next iteration
+    __syncthreads();  // stage buffers, Sb and VN are rewritten next iteration
+    for (int i = tid; i < L * (kScanBV / 8); i += kScanThreads) {
+      const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
+      *reinterpret_cast<uint4*>(o + ((t0 + r) * H + h) * V + v0 + p) = *reinterpret_cast<const uint4*>(&sm.O[r][p]);
+    }
   }
   cp_async_wait<0>();
 

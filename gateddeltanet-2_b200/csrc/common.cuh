@@ -135,6 +135,53 @@ GDN2_DEV void warp_mma(float (&acc)[MT][NT][4], Smem A, int m0, Smem B, int n0, 
   }
 }
 
+// Same product with the reduction split over KS independent accumulator sets
+// (k-steps dealt round-robin) that are summed at the end: a dependent chain
+// of k_len/16/KS tensor-core ops instead of k_len/16, for latency-bound loops.
+template <int KS, int MT, int NT, bool kATrans, bool kBNK>
+GDN2_DEV void warp_mma_ks(float (&acc)[MT][NT][4], Smem A, int m0, Smem B, int n0, int k_begin, int k_end,
+                          int lane) {
+  static_assert(NT % 2 == 0, "NT must be even");
+  float part[KS][MT][NT][4];
+#pragma unroll
+  for (int s = 0; s < KS; ++s)
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) part[s][i][j][e] = 0.f;
+  for (int k0 = k_begin; k0 < k_end; k0 += 16 * KS) {
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      const int kk = k0 + 16 * s;
+      if (kk < k_end) {
+        uint32_t af[MT][4];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) load_a<kATrans>(af[i], A, m0 + 16 * i, kk, lane);
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) {
+          uint32_t bf[4];
+          load_b2<kBNK>(bf, B, kk, n0 + 8 * j, lane);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            mma_bf16(part[s][i][j], af[i], bf);
+            mma_bf16(part[s][i][j + 1], af[i], bf + 2);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < KS; ++s)
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][j][e] += part[s][i][j][e];
+}
+
 template <int MT, int NT>
 GDN2_DEV void zero_acc(float (&acc)[MT][NT][4]) {
 #pragma unroll
