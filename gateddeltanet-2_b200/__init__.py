@@ -18,7 +18,7 @@ registers the alias ``gdn2_b200`` so later ``import gdn2_b200`` works.
 
 import sys as _sys
 
-from . import _lib
+from . import _lib, cp
 from .chunk import ChunkGDN2Function, chunk_gdn2, gdn2_telemetry_snapshot, prepare_chunk_indices
 from .recurrent import fused_recurrent_gdn2, fused_recurrent_gdn2_fwd
 
@@ -31,4 +31,5 @@ __all__ = [
     "fused_recurrent_gdn2_fwd",
     "prepare_chunk_indices",
     "gdn2_telemetry_snapshot",
+    "cp",
 ]

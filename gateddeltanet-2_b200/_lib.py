@@ -107,7 +107,7 @@ def load() -> ctypes.CDLL:
     lib.gdn2_recurrent_fwd.restype = ctypes.c_int
     lib.gdn2_cp_transition.argtypes = [ctypes.POINTER(ChunkArgs), _p, _p, ctypes.c_size_t, _p]
     lib.gdn2_cp_transition.restype = ctypes.c_int
-    lib.gdn2_cp_compose.argtypes = [_p, _i32, _i64, _i64, _i64, _p, _p]
+    lib.gdn2_cp_compose.argtypes = [_p, _i32, _i64, _i64, _i64, _i64, _p, _p]
     lib.gdn2_cp_compose.restype = ctypes.c_int
     lib.gdn2_status_string.argtypes = [ctypes.c_int]
     lib.gdn2_status_string.restype = ctypes.c_char_p

@@ -453,7 +453,7 @@ struct ScanSmem {
 
 template <int K, int V>
 GDN2_DEV void scan_prefetch(ScanStage<K>& st, const ChunkWs& ws, const gdn2_chunk_args& a, int64_t t0, int L,
-                            int64_t h, int v0, int tid) {
+                            int64_t h, int v0, int tid, bool zero_u = false) {
   const int64_t H = a.H;
   // rows of K bf16 = K/8 16-byte pieces
   for (int i = tid; i < kChunk * (K / 8); i += kScanThreads) {
@@ -472,20 +472,28 @@ GDN2_DEV void scan_prefetch(ScanStage<K>& st, const ChunkWs& ws, const gdn2_chun
   for (int i = tid; i < kChunk * (kScanBV / 8); i += kScanThreads) {
     const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
     const bool ok = r < L;
-    cp_async16(&st.U[r][p], ws.U + ((t0 + (ok ? r : 0)) * H + h) * V + v0 + p, ok);
+    cp_async16(&st.U[r][p], ws.U + ((t0 + (ok ? r : 0)) * H + h) * V + v0 + p, ok && !zero_u);
   }
   for (int i = tid; i < K / 4; i += kScanThreads)
     cp_async16(&st.glast[i * 4], ws.G + ((t0 + L - 1) * H + h) * K + i * 4, true);
 }
 
-template <int K, int V>
+// kTrans: context-parallel transition pass.  The grid then covers K + V
+// columns of the augmented state [S_M | S]: the first K columns start at the
+// identity and see U = 0, so they end as the shard's transition matrix
+// M = prod_c (Diag(2^G_last) - kg^T Y); the last V start from the given
+// initial state (or zero) and end as the shard's exit state h_e.  Both are
+// written to maps[n, h, :, 0:K] and maps[n, h, :, K:K+V]; no output is formed.
+template <int K, int V, bool kTrans>
 __global__ void __launch_bounds__(kScanThreads, 1)
-chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
+chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   ScanSmem<K>& sm = *reinterpret_cast<ScanSmem<K>*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t H = a.H;
-  const int v0 = blockIdx.x * kScanBV;
+  const bool is_m = kTrans && blockIdx.x < K / kScanBV;  // transition columns
+  const int mcol0 = is_m ? blockIdx.x * kScanBV : 0;
+  const int v0 = kTrans ? (is_m ? 0 : (int)(blockIdx.x - K / kScanBV) * kScanBV) : blockIdx.x * kScanBV;
   const int64_t n = blockIdx.y / H, h = blockIdx.y % H;
   SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
   int64_t bos, len;
@@ -493,7 +501,7 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
   const int64_t nchunks = (len + kChunk - 1) / kChunk;
   const int64_t c0 = geo.chunk0(n);
   const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
-  const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  const bool save = !kTrans && (a.flags & GDN2_SAVE_FOR_BWD);
   __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.o);
 
   // state accumulators: warp w owns rows [16w, 16w+16) (K=128: 8 warps) x 64 cols
@@ -507,7 +515,9 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
   const int sr0 = srows ? sm0 : warp * 16;
   acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
     float x = 0.f;
-    if (sown && (a.flags & GDN2_HAS_H0)) {
+    if (is_m) {
+      x = (r == mcol0 + c) ? 1.f : 0.f;
+    } else if (sown && (a.flags & GDN2_HAS_H0)) {
       const float* h0 = a.h0 + (n * H + h) * (int64_t)K * V;
       x = tr ? h0[(int64_t)(v0 + c) * K + r] : h0[(int64_t)r * V + v0 + c];
     }
@@ -516,7 +526,7 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
 
   if (nchunks > 0) {
     const int L0 = (int)(kChunk < (len) ? (int64_t)kChunk : (len));
-    scan_prefetch<K, V>(sm.st[0], ws, a, bos, L0, h, v0, tid);
+    scan_prefetch<K, V>(sm.st[0], ws, a, bos, L0, h, v0, tid, is_m);
   }
   cp_async_commit();
 
@@ -528,7 +538,7 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
     if (sown) acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) { sm.Sb[r][c] = __float2bfloat16_rn(v); });
     if (ci + 1 < nchunks) {
       const int Ln = (int)(kChunk < (len - (ci + 1) * kChunk) ? (int64_t)kChunk : (len - (ci + 1) * kChunk));
-      scan_prefetch<K, V>(sm.st[(ci + 1) & 1], ws, a, t0 + kChunk, Ln, h, v0, tid);
+      scan_prefetch<K, V>(sm.st[(ci + 1) & 1], ws, a, t0 + kChunk, Ln, h, v0, tid, is_m);
     }
     cp_async_commit();
     cp_async_wait<1>();
@@ -561,7 +571,7 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
       }
     }
     // o = scale * qg S + Aqk v_new
-    {
+    if (!kTrans) {
       float acc[1][4][4];
       zero_acc(acc);
       warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.QG[0][0], ScanStage<K>::LK}, m0,
@@ -588,13 +598,22 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws) {
                                     0, 0, kChunk, lane);
     }
     __syncthreads();  // stage buffers, Sb and VN are rewritten next iteration
-    for (int i = tid; i < L * (kScanBV / 8); i += kScanThreads) {
+    for (int i = tid; i < (kTrans ? 0 : L) * (kScanBV / 8); i += kScanThreads) {
       const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
       *reinterpret_cast<uint4*>(o + ((t0 + r) * H + h) * V + v0 + p) = *reinterpret_cast<const uint4*>(&sm.O[r][p]);
     }
   }
   cp_async_wait<0>();
 
+  if (kTrans) {
+    if (sown) {
+      float* mp = maps + (n * H + h) * (int64_t)K * (K + V);
+      acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
+        mp[(int64_t)r * (K + V) + (is_m ? mcol0 + c : K + v0 + c)] = v;
+      });
+    }
+    return;
+  }
   if (sown && (a.flags & GDN2_STORE_FINAL)) {
     float* ht = a.ht + (n * H + h) * (int64_t)K * V;
     acc_foreach(S, sr0, 0, lane, [&](float& v, int r, int c) {
@@ -617,13 +636,41 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
     GDN2_LAUNCH_CHECK();
   }
   const size_t sm2 = sizeof(ScanSmem<K>);
-  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sm2));
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
   dim3 g2((unsigned)(V / kScanBV), (unsigned)(a.N * a.H));
   ProfScope ps(kKScanFwd, s);
-  chunk_scan_fwd_kernel<K, V><<<g2, kScanThreads, sm2, s>>>(a, ws);
+  chunk_scan_fwd_kernel<K, V, false><<<g2, kScanThreads, sm2, s>>>(a, ws, nullptr);
   GDN2_LAUNCH_CHECK();
   return 0;
+}
+
+template <int K, int V>
+int launch_transition_kv(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s) {
+  if (a.NT > 0) {
+    const size_t sm1 = sizeof(IntraSmem<K, V>);
+    auto k1 = a.dtype_bw == GDN2_BF16 ? chunk_intra_kernel<K, V, __nv_bfloat16> : chunk_intra_kernel<K, V, float>;
+    GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
+    dim3 g1((unsigned)a.NT, (unsigned)a.H);
+    ProfScope ps(kKIntra, s);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
+    GDN2_LAUNCH_CHECK();
+  }
+  const size_t sm2 = sizeof(ScanSmem<K>);
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));
+  dim3 g2((unsigned)((K + V) / kScanBV), (unsigned)(a.N * a.H));
+  ProfScope ps(kKCp, s);
+  chunk_scan_fwd_kernel<K, V, true><<<g2, kScanThreads, sm2, s>>>(a, ws, maps);
+  GDN2_LAUNCH_CHECK();
+  return 0;
+}
+
+int chunk_transition_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s) {
+  if (a.K == 128 && a.V == 128) return launch_transition_kv<128, 128>(a, ws, maps, s);
+  if (a.K == 128 && a.V == 64) return launch_transition_kv<128, 64>(a, ws, maps, s);
+  if (a.K == 64 && a.V == 128) return launch_transition_kv<64, 128>(a, ws, maps, s);
+  return launch_transition_kv<64, 64>(a, ws, maps, s);
 }
 
 int chunk_fwd_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {

@@ -87,6 +87,7 @@ inline size_t bwd_ws_layout(const gdn2_chunk_args& a, void* base, BwdWs* ws) {
 GDN2_DEV constexpr int anchor_row0(int i) { return 8 * i * (i + 1); }
 
 int chunk_fwd_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
+int chunk_transition_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s);
 int chunk_bwd_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
                      cudaStream_t s);
 int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s);

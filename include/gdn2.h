@@ -201,20 +201,25 @@ int gdn2_recurrent_fwd(const gdn2_recurrent_args* a, gdn2_stream_t stream);
 /* context parallel (T sharded over ranks)                                   */
 /* ------------------------------------------------------------------------- */
 /*
- * A shard of one sequence maps its incoming state affinely:
- *     S_out = M S_in + h_e,  M in R^{K x K}, h_e in R^{K x V}  (per head)
- * gdn2_cp_transition computes [M | h_e] for a shard (gate activation, l2norm
- * and the WY factors as in gdn2_chunk_fwd), packed as [H, K, K+V] fp32.  This
- * mirrors the KDA context-parallel pre-process of the reference
- * (chunk_kda.py:102-330 pre_process_fwd_kernel_merged, :774-852) which
- * GDN2 shares the scan kernels with but never wires up (chunk_gdn2.py:86-92).
- * gdn2_cp_compose folds the maps of ranks 0..rank-1 (gathered as
- * [world, H, K, K+V]) into this rank's initial state (chunk_kda.py:465-477).
+ * A shard of a sequence maps the state it receives affinely (per head):
+ *     S_out = M S_in + h_e,  M in R^{K x K}, h_e in R^{K x V}
+ * gdn2_cp_transition computes [M | h_e] for each sequence of a dense shard
+ * (gate activation, l2norm and the WY factors as in gdn2_chunk_fwd; h_e from
+ * the given initial state, or zero), packed as maps[N, H, K, K+V] fp32 (M in
+ * columns 0..K-1).  It needs the workspace gdn2_chunk_workspace_size reports
+ * for the same arguments (without GDN2_SAVE_FOR_BWD).  This mirrors the KDA
+ * context-parallel pre-process of the reference (chunk_kda.py:102-330,
+ * :774-852), which GDN2 shares the scan kernels with but never enables
+ * (chunk_gdn2.py:86-92).
+ * gdn2_cp_compose folds the maps of ranks 0..rank-1, gathered as
+ * [world, N, H, K, K+V], into `state` [N, H, K, V] fp32 in place: on entry the
+ * sequence's initial state (or zeros), on return this rank's entering state
+ * (S <- M_j S + h_j in rank order; chunk_kda.py:465-477).
  */
 int gdn2_cp_transition(const gdn2_chunk_args* a, float* maps, void* workspace,
                        size_t workspace_bytes, gdn2_stream_t stream);
-int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t H, int64_t K, int64_t V,
-                    float* h0_out, gdn2_stream_t stream);
+int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t N, int64_t H, int64_t K,
+                    int64_t V, float* state, gdn2_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* opt-in per-kernel timing (measurement hook, no reference counterpart)     */
