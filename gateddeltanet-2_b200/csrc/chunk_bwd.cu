@@ -202,7 +202,6 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
 // 16 warps: warp w owns rows [16 (w & 3), +16) and columns [(w >> 2) K/4, +K/4)
 // of every [64 x K] accumulator (dq, dk, db, dG), 16 fp32 registers each.
 constexpr int kBIntraThreads = 512;
-constexpr int kBIntraWarps = kBIntraThreads / 32;
 constexpr float kAnchorRangeB = 96.f;  // must match the forward's anchored range
 
 template <int K, int V, typename TB>
@@ -217,6 +216,7 @@ struct BIntraSmem {
   alignas(16) float last[K];               // dgk_last + sum_r k dk_inter
   alignas(16) float rsum[kChunk][4][2];    // l2norm row sums (q, k) per column group
   alignas(16) uint8_t flag[4][K];
+  alignas(16) float ptot[kBIntraThreads / K][K];  // per-part sums of the dg reverse cumsum
   int nflag;
   // phase 1 needs h, dh, do, v_new, dv_new; phase 2 the WY operands; phase 3
   // the anchored score operands.  q, k, b are staged once phase 1's products
@@ -265,6 +265,15 @@ using BIntraSmem64x64 = BIntraSmem<64, 64, float>;
 static_assert(offsetof(BIntraSmem64x64, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
 using BScanSmem128 = BScanSmem<128>;
 static_assert(offsetof(BScanSmem128, DSb) % 16 == 0 && sizeof(BScanStage<128>) % 16 == 0, "stage alignment");
+
+template <typename TB>
+GDN2_DEV void store2(TB* p, float x0, float x1);
+template <>
+GDN2_DEV void store2<float>(float* p, float x0, float x1) { *reinterpret_cast<float2*>(p) = make_float2(x0, x1); }
+template <>
+GDN2_DEV void store2<__nv_bfloat16>(__nv_bfloat16* p, float x0, float x1) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(x0, x1);
+}
 
 template <typename TB>
 GDN2_DEV float ldb(const void* p, int64_t i) {
@@ -401,12 +410,9 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     cp_async16b(&sg.Bg[r][p], static_cast<const TB*>(a.b) + tokK(ok ? r : 0, p), ok);
   }
   cp_commit();
-  // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv)   (overlaps the staging)
+  // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv); the same registers of
+  // w and v also form WV = w v for phase 2 (w, v are read from HBM once)
   {
-    float t[1][NTv][4];
-    zero_acc(t);
-    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
-                                  lane);
     __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
     TB* dw = static_cast<TB*>(gr.dw);
     float wl[NTv][4], vl[NTv][4];
@@ -418,15 +424,22 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         wl[j][e] = r < L ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
         vl[j][e] = r < L ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
       }
+    float t[1][NTv][4];
+    zero_acc(t);
+    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
+                                  lane);
 #pragma unroll
     for (int j = 0; j < NTv; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0v + 8 * j + 2 * (lane & 3) + (e & 1);
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0v + 8 * j + 2 * (lane & 3);
+        *reinterpret_cast<__nv_bfloat162*>(&p2.WV[r][c]) =
+            __floats2bfloat162_rn(wl[j][2 * x] * vl[j][2 * x], wl[j][2 * x + 1] * vl[j][2 * x + 1]);
         if (r < L) {
           const int64_t gi = tokV(r, c);
-          dv[gi] = __float2bfloat16_rn(t[0][j][e] * wl[j][e]);
-          dw[gi] = from_f<TB>(t[0][j][e] * vl[j][e]);
+          *reinterpret_cast<__nv_bfloat162*>(dv + gi) =
+              __floats2bfloat162_rn(t[0][j][2 * x] * wl[j][2 * x], t[0][j][2 * x + 1] * wl[j][2 * x + 1]);
+          store2<TB>(dw + gi, t[0][j][2 * x] * vl[j][2 * x], t[0][j][2 * x + 1] * vl[j][2 * x + 1]);
         }
       }
   }
@@ -467,20 +480,6 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   for (int i = tid; i < kChunk * K; i += kBIntraThreads) {
     const int r = i / K, c = i % K;
     p2.KB2G[r][c] = __float2bfloat16_rn(bv(r, c) * kv(r, c) * exp2_approx(sm.G[r][c]));
-  }
-  for (int i0 = tid; i0 < kChunk * V; i0 += 8 * kBIntraThreads) {
-    float w8[8], v8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
-      w8[u] = (i < kChunk * V && r < L) ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
-      v8[u] = (i < kChunk * V && r < L) ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * kBIntraThreads, r = i / V, c = i % V;
-      if (i < kChunk * V) p2.WV[r][c] = __float2bfloat16_rn(w8[u] * v8[u]);
-    }
   }
   __syncthreads();
   {
@@ -661,36 +660,50 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
         if (r >= L) continue;
         const int64_t gi = tokK(r, c);
-        float xq = dq[0][j][e], xk = dk[0][j][e];
+        float xq0 = dq[0][j][2 * x], xq1 = dq[0][j][2 * x + 1];
+        float xk0 = dk[0][j][2 * x], xk1 = dk[0][j][2 * x + 1];
         if (l2) {
           float sq = 0.f, sk = 0.f;
 #pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            sq += sm.rsum[r][x][0];
-            sk += sm.rsum[r][x][1];
+          for (int y = 0; y < 4; ++y) {
+            sq += sm.rsum[r][y][0];
+            sk += sm.rsum[r][y][1];
           }
           const float rq = ws.q_rstd[(t0 + r) * H + h], rk = ws.k_rstd[(t0 + r) * H + h];
-          xq = (xq - sq * qv(r, c)) * rq;
-          xk = (xk - sk * kv(r, c)) * rk;
+          xq0 = (xq0 - sq * qv(r, c)) * rq;
+          xq1 = (xq1 - sq * qv(r, c + 1)) * rq;
+          xk0 = (xk0 - sk * kv(r, c)) * rk;
+          xk1 = (xk1 - sk * kv(r, c + 1)) * rk;
         }
-        dqo[gi] = __float2bfloat16_rn(xq);
-        dko[gi] = __float2bfloat16_rn(xk);
-        dbo[gi] = from_f<TB>(db[0][j][e]);
+        *reinterpret_cast<__nv_bfloat162*>(dqo + gi) = __floats2bfloat162_rn(xq0, xq1);
+        *reinterpret_cast<__nv_bfloat162*>(dko + gi) = __floats2bfloat162_rn(xk0, xk1);
+        store2<TB>(dbo + gi, db[0][j][2 * x], db[0][j][2 * x + 1]);
       }
   }
-  // dg: reverse cumsum inside the chunk, then the gate VJP
+  // dg: reverse cumsum inside the chunk, then the gate VJP.  All threads take
+  // part: channel c = tid % K, row part p = tid / K (kParts parts of the chunk).
   const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
   const bool lbnd = a.flags & GDN2_LOWER_BOUND;
-  for (int c = tid; c < K; c += kBIntraThreads) {
+  {
+    constexpr int kParts = kBIntraThreads / K, kRowsPer = kChunk / kParts;
+    const int c = tid % K, p = tid / K;
+    const int r_lo = p * kRowsPer, r_hi = r_lo + kRowsPer;  // rows [r_lo, r_hi)
+    float part = 0.f;
+    for (int r = r_lo; r < r_hi; ++r) part += sm.G[r][c];  // rows >= L hold zero
+    sm.ptot[p][c] = part;
+    __syncthreads();
+    float acc = 0.f;
+    for (int q2 = p + 1; q2 < kParts; ++q2) acc += sm.ptot[q2][c];
     const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
     const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
-    float acc = 0.f, dA = 0.f, dbias = 0.f;
-    for (int r = L - 1; r >= 0; --r) {
+    float dA = 0.f, dbias = 0.f;
+    for (int r = r_hi - 1; r >= r_lo; --r) {
       acc += sm.G[r][c];
+      if (r >= L) continue;
       const int64_t gi = tokK(r, c);
       float out = acc;
       if (gate) {
@@ -711,7 +724,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       if (a.dt_bias) atomicAdd(&gr.ddt_bias[h * K + c], dbias);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) dA += __shfl_xor_sync(0xffffffffu, dA, off);
-      if ((c & 31) == 0) atomicAdd(&gr.dA_log[h], dA);
+      if (lane == 0) atomicAdd(&gr.dA_log[h], dA);
     }
   }
 }
