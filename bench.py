@@ -14,6 +14,8 @@ the same run and reported under ``decode``.
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
 (multi-GPU through ``torch.distributed.run``; one rank per GPU).
+``--batch`` / ``--decode-seqs`` shrink the two workloads for ncu captures; a
+line measured with either changed is not a config-2 / config-3 number.
 ``--impl reference`` times the reference's algorithm on the host cores (the
 oracle port: the reference has no CPU implementation of its own and its
 kernels are Triton/sm_120 CUDA); it runs on rank 0 only.
@@ -54,8 +56,8 @@ KERNEL_BYTES_PER_TOKEN_HEAD = {
     + 2 * 2 * 128 + 2 * 4 * 128 + 2 * 128 + 3 * 2 * 128 + 3 * 4 * 128,
 }
 # decode: fp32 state read + write per (sequence, head) plus per-token vectors
-DECODE_BYTES_PER_STEP = (2 * DEC_N * H * K * V * 4 + DEC_N * H * (3 * 2 * 128 + 3 * 4 * 128)
-                         + DEC_N * H * V * 2)
+def decode_bytes_per_step(n):
+    return 2 * n * H * K * V * 4 + n * H * (3 * 2 * 128 + 3 * 4 * 128) + n * H * V * 2
 
 
 def parse():
@@ -66,6 +68,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--decode-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=B,
+                    help="sequences per GPU (config 2 is 4; smaller values are for ncu captures)")
+    ap.add_argument("--decode-seqs", type=int, default=DEC_N,
+                    help="decode sequences per GPU (config 3 is 256; smaller for ncu captures)")
     return ap.parse_args()
 
 
@@ -78,13 +84,22 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "dram_traffic_per_launch_config2_config3.txt")
+
+
 def traffic_table():
-    """DRAM bytes per launch from committed ncu summaries (profiles/traffic.json)."""
+    """DRAM bytes (read + write) per launch at the full config-2 / config-3
+    sizes, from the committed ncu summary: lines ``traffic <kernel> <bytes>``."""
+    out = {}
     try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f)
-    except Exception:
-        return {}
+        with open(TRAFFIC_FILE) as f:
+            for ln in f:
+                parts = ln.split()
+                if len(parts) == 3 and parts[0] == "traffic":
+                    out[parts[1]] = int(parts[2])
+    except OSError:
+        pass
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -192,6 +207,8 @@ def cpu_baseline_ours():
 # ---------------------------------------------------------------------------
 def main():
     args = parse()
+    nb, nd = args.batch, args.decode_seqs
+    dec_bytes = decode_bytes_per_step(nd)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -221,13 +238,13 @@ def main():
     def rnd(*shape):
         return torch.randn(*shape, device=dev, generator=gen)
 
-    q = F.normalize(rnd(B, T, H, K), dim=-1).bfloat16()
-    k = F.normalize(rnd(B, T, H, K), dim=-1).bfloat16()
-    v = rnd(B, T, H, V).bfloat16()
-    g = -F.softplus(rnd(B, T, H, K)) * 0.1
-    b = torch.sigmoid(rnd(B, T, H, K))
-    w = torch.sigmoid(rnd(B, T, H, V))
-    do = rnd(B, T, H, V).bfloat16()
+    q = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
+    k = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
+    v = rnd(nb, T, H, V).bfloat16()
+    g = -F.softplus(rnd(nb, T, H, K)) * 0.1
+    b = torch.sigmoid(rnd(nb, T, H, K))
+    w = torch.sigmoid(rnd(nb, T, H, V))
+    do = rnd(nb, T, H, V).bfloat16()
     leaves = [x.requires_grad_(True) for x in (q, k, v, g, b, w)]
 
     def step():
@@ -266,7 +283,7 @@ def main():
     _lib.profile_enable(False)
     clk = clocks.stop()
     gpu_launches = sum(n for n, _ in prof.values())
-    tok_per_step = world * B * T
+    tok_per_step = world * nb * T
     value = tok_per_step * args.steps / (ms / 1e3)
 
     # ---- end to end through the public API: pinned host inputs -> device ----
@@ -296,13 +313,13 @@ def main():
                    "memory each step, loss scalar read back"}
 
     # ---- decode (config 3): in-place state update, 1 token per sequence --------
-    S = rnd(DEC_N, H, K, V) * 0.02
+    S = rnd(nd, H, K, V) * 0.02
     ring = []
     for i in range(4):
-        ring.append((F.normalize(rnd(DEC_N, 1, H, K), dim=-1).bfloat16(),
-                     F.normalize(rnd(DEC_N, 1, H, K), dim=-1).bfloat16(),
-                     rnd(DEC_N, 1, H, V).bfloat16(), -F.softplus(rnd(DEC_N, 1, H, K)) * 0.1,
-                     torch.sigmoid(rnd(DEC_N, 1, H, K)), torch.sigmoid(rnd(DEC_N, 1, H, V))))
+        ring.append((F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
+                     F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
+                     rnd(nd, 1, H, V).bfloat16(), -F.softplus(rnd(nd, 1, H, K)) * 0.1,
+                     torch.sigmoid(rnd(nd, 1, H, K)), torch.sigmoid(rnd(nd, 1, H, V))))
     it = [0]
 
     def dec_step():
@@ -318,29 +335,29 @@ def main():
     _lib.profile_enable(False)
     peak, peak_kind = peaks()
     dec_us = 1e3 * dec_ms / args.decode_steps
-    dec_gbs = DECODE_BYTES_PER_STEP / (dec_us * 1e-6) / 1e9
+    dec_gbs = dec_bytes / (dec_us * 1e-6) / 1e9
     dk = dprof.get("recurrent_kernel", (1, dec_ms))
     dk_us = 1e3 * dk[1] / max(dk[0], 1)
     decode = {"metric": "decode-step state HBM GB/s", "value": world * dec_gbs, "unit": "GB/s",
-              "us_per_step": dec_us, "tokens_per_s": world * DEC_N / (dec_us * 1e-6),
-              "config": {"workload": "config3 decode step", "sequences_per_gpu": DEC_N, "heads": H,
-                         "state": "fp32 [256,16,128,128] in place", "steps": args.decode_steps},
-              "roofline": {"bound": "hbm", "achieved": DECODE_BYTES_PER_STEP / (dk_us * 1e-6) / 1e9,
+              "us_per_step": dec_us, "tokens_per_s": world * nd / (dec_us * 1e-6),
+              "config": {"workload": "config3 decode step", "sequences_per_gpu": nd, "heads": H,
+                         "state": f"fp32 [{nd},16,128,128] in place", "steps": args.decode_steps},
+              "roofline": {"bound": "hbm", "achieved": dec_bytes / (dk_us * 1e-6) / 1e9,
                            "peak": peak, "unit": "GB/s",
-                           "frac": DECODE_BYTES_PER_STEP / (dk_us * 1e-6) / 1e9 / peak,
+                           "frac": dec_bytes / (dk_us * 1e-6) / 1e9 / peak,
                            "peak_source": peak_kind, "kernel": "recurrent_kernel",
                            "us_per_launch": dk_us,
-                           "traffic": traffic_table().get("recurrent_kernel")}}
+                           "traffic": traffic_table().get("recurrent_kernel") if nd == DEC_N else None}}
 
     # ---- roofline of the dominant kernel of the fwd+bwd step ------------------
     dom = max(prof.items(), key=lambda kv: kv[1][1])
     name, (nl, tms) = dom
     per_launch_s = tms / nl / 1e3
-    alg = KERNEL_BYTES_PER_TOKEN_HEAD[name] * B * T * H
+    alg = KERNEL_BYTES_PER_TOKEN_HEAD[name] * nb * T * H
     achieved = alg / per_launch_s / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": peak_kind,
-                "traffic": traffic_table().get(name), "kernel": name,
+                "traffic": traffic_table().get(name) if nb == B else None, "kernel": name,
                 "algorithmic_bytes_per_launch": alg, "us_per_launch": per_launch_s * 1e6,
                 "kernel_shares": {n: round(t / sum(x[1] for x in prof.values()), 4)
                                   for n, (c, t) in prof.items()}}
@@ -351,10 +368,10 @@ def main():
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "config2: GDN2 op fwd+bwd, B=4 H=16 T=4096 dk=dv=128 chunk 64 per GPU",
-                       "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": K,
+            "config": {"workload": f"config2: GDN2 op fwd+bwd, B={nb} H=16 T=4096 dk=dv=128 chunk 64 per GPU",
+                       "global_batch": nb * world, "seq_len": T, "heads": H, "head_dim": K,
                        "parallelism": f"(batch x head) shards, {world} GPU(s), no collectives",
-                       "l2": "inputs 0.60 GB per GPU per step (> 126 MB L2), no flush needed",
+                       "l2": f"inputs {0.15 * nb:.2f} GB per GPU per step (> 126 MB L2), no flush needed",
                        "gates": "b, w, log-decay fp32; q, k, v bf16"},
             "clocks": clk, "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline,
             "decode": decode,
