@@ -49,6 +49,8 @@ KERNEL_BYTES_PER_TOKEN_HEAD = {
     "chunk_intra_kernel": 3 * 2 * 128 + 3 * 4 * 128 + 4 * 128 + 2 * 2 * 64 + 4 * 2 * 128,
     # reads Y, qg, kg, U, Aqk; writes o, v_new and the chunk states h (K*V bf16 / 64 tokens)
     "chunk_scan_fwd_kernel": 4 * 2 * 128 + 2 * 64 + 2 * 2 * 128 + (128 * 128 * 2) // 64,
+    # the same interface, on tcgen05 tensor cores (d_k = d_v = 128)
+    "chunk_scan_fwd_tc_kernel": 4 * 2 * 128 + 2 * 64 + 2 * 2 * 128 + (128 * 128 * 2) // 64,
     # reads Y, qg, kg, Aqk, do; writes dh (K*V bf16 / 64 tokens) and dv_new
     "chunk_scan_bwd_kernel": 3 * 2 * 128 + 2 * 64 + 2 * 128 + (128 * 128 * 2) // 64 + 2 * 128,
     # reads h, dh, do, v_new, dv_new, A, G, q, k, b, w, v; writes dq, dk, dv, dg, db, dw

@@ -80,7 +80,7 @@ EXPORTS = (
     "gdn2_chunk_workspace_size", "gdn2_chunk_bwd_workspace_size", "gdn2_chunk_fwd",
     "gdn2_chunk_bwd", "gdn2_recurrent_fwd", "gdn2_cp_transition", "gdn2_cp_compose",
     "gdn2_status_string", "gdn2_device_supported", "gdn2_abi_version",
-    "gdn2_profile_enable", "gdn2_profile_read",
+    "gdn2_profile_enable", "gdn2_profile_read", "gdn2_device_fault_read",
 )
 
 
@@ -119,6 +119,8 @@ def load() -> ctypes.CDLL:
     lib.gdn2_profile_read.restype = ctypes.c_int
     lib.gdn2_abi_version.argtypes = []
     lib.gdn2_abi_version.restype = ctypes.c_int
+    lib.gdn2_device_fault_read.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    lib.gdn2_device_fault_read.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -167,3 +169,13 @@ def profile_read() -> dict:
     if n < 0:
         check(n, "gdn2_profile_read")
     return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(n)}
+
+
+def device_fault_read(clear: bool = True) -> int:
+    """Fault word of the current device: bit 0 = a bounded wait inside a
+    tensor-core kernel gave up (its results are invalid).  Synchronises."""
+    import torch
+    torch.cuda.synchronize()
+    out = ctypes.c_uint(0)
+    check(load().gdn2_device_fault_read(1 if clear else 0, ctypes.byref(out)), "gdn2_device_fault_read")
+    return int(out.value)

@@ -55,10 +55,16 @@ const char* gdn2_status_string(int s) {
     case GDN2_ERR_NO_DEVICE: return "no sm_100 device";
     case GDN2_ERR_SCRATCH_LIMIT:
       return "problem needs more than the 32 MiB built-in scratch; use gdn2_chunk_fwd with a caller workspace";
+    case GDN2_ERR_TENSOR_MAP: return "cuTensorMapEncodeTiled unavailable or rejected a workspace array";
     default: break;
   }
   if (s < 0) return cudaGetErrorString(static_cast<cudaError_t>(-s));
   return "unknown status";
+}
+
+int gdn2_device_fault_read(int clear, unsigned int* out) {
+  if (!out) return GDN2_ERR_NULL_POINTER;
+  return gdn2::tc_fault_read(clear, out);
 }
 
 int gdn2_device_supported(int device) {

@@ -224,7 +224,7 @@ struct BIntraSmem {
   struct P1 {
     alignas(16) __nv_bfloat16 DVN[kChunk][LV];
     alignas(16) __nv_bfloat16 DY[kChunk][LK];
-    alignas(16) __nv_bfloat16 Hs[K][LV];
+    alignas(16) __nv_bfloat16 HsT[V][LK];  // h^T: the chunk's entering state, [v][k]
     alignas(16) __nv_bfloat16 DH[K][LV];
     alignas(16) __nv_bfloat16 DO[kChunk][LV];
     alignas(16) __nv_bfloat16 VN[kChunk][LV];
@@ -314,9 +314,12 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   {
     const __nv_bfloat16* hsrc = ws.h + (cidx * H + h) * (int64_t)K * V;
     const __nv_bfloat16* dhsrc = bw.dh + (cidx * H + h) * (int64_t)K * V;
+    for (int i = tid; i < V * (K / 8); i += kBIntraThreads) {
+      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+      cp_async16b(&p1.HsT[r][p], hsrc + (int64_t)r * K + p, true);
+    }
     for (int i = tid; i < K * (V / 8); i += kBIntraThreads) {
       const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      cp_async16b(&p1.Hs[r][p], hsrc + (int64_t)r * V + p, true);
       cp_async16b(&p1.DH[r][p], dhsrc + (int64_t)r * V + p, true);
     }
     for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
@@ -366,12 +369,12 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   const float* Glast = &sm.G[kChunk - 1][0];
 
   // ---- phase 1: products with h, dh ------------------------------------------
-  warp_mma<1, NTk, false, true>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.Hs[0][0], S::LV}, n0, 0, V, lane);
+  warp_mma<1, NTk, false, false>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
   warp_mma<1, NTk, false, true>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DH[0][0], S::LV}, n0, 0, V, lane);
   {
     float t[1][NTk][4];
     zero_acc(t);
-    warp_mma<1, NTk, false, true>(t, Smem{&p1.DVN[0][0], S::LV}, m0, Smem{&p1.Hs[0][0], S::LV}, n0, 0, V, lane);
+    warp_mma<1, NTk, false, false>(t, Smem{&p1.DVN[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
     acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { p1.DY[r][c] = __float2bfloat16_rn(-v); });
   }
   // dgk_last = 2^G_last * sum_v h dh  (4 threads per state row)
@@ -380,7 +383,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     float s = 0.f;
     if (r < K) {
       for (int v = part * (V / 4); v < (part + 1) * (V / 4); ++v)
-        s += __bfloat162float(p1.Hs[r][v]) * __bfloat162float(p1.DH[r][v]);
+        s += __bfloat162float(p1.HsT[v][r]) * __bfloat162float(p1.DH[r][v]);
     }
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);

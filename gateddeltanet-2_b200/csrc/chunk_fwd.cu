@@ -543,11 +543,16 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    if (save) {  // the chunk's entering state h, 16-byte stores out of Sb
-      __nv_bfloat16* hdst = ws.h + ((c0 + ci) * H + h) * (int64_t)K * V + v0;
-      for (int i = tid; i < K * (kScanBV / 8); i += kScanThreads) {
-        const int r = i / (kScanBV / 8), p = (i % (kScanBV / 8)) * 8;
-        *reinterpret_cast<uint4*>(hdst + (int64_t)r * V + p) = *reinterpret_cast<const uint4*>(&sm.Sb[r][p]);
+    if (save) {  // the chunk's entering state, transposed (h^T [v][k]), 16-byte stores
+      __nv_bfloat16* hdst = ws.h + ((c0 + ci) * H + h) * (int64_t)K * V + (int64_t)v0 * K;
+      for (int i = tid; i < kScanBV * (K / 8); i += kScanThreads) {
+        const int c = i / (K / 8), p = (i % (K / 8)) * 8;
+        uint4 pk;
+        pk.x = pack_bf16(__bfloat162float(sm.Sb[p + 0][c]), __bfloat162float(sm.Sb[p + 1][c]));
+        pk.y = pack_bf16(__bfloat162float(sm.Sb[p + 2][c]), __bfloat162float(sm.Sb[p + 3][c]));
+        pk.z = pack_bf16(__bfloat162float(sm.Sb[p + 4][c]), __bfloat162float(sm.Sb[p + 5][c]));
+        pk.w = pack_bf16(__bfloat162float(sm.Sb[p + 6][c]), __bfloat162float(sm.Sb[p + 7][c]));
+        *reinterpret_cast<uint4*>(hdst + (int64_t)c * K + p) = pk;
       }
     }
 
@@ -635,6 +640,7 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
     k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
     GDN2_LAUNCH_CHECK();
   }
+  if (scan_fwd_tc_supported(a)) return scan_fwd_tc_launch(a, ws, s);
   const size_t sm2 = sizeof(ScanSmem<K>);
   GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V, false>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));

@@ -13,7 +13,8 @@ namespace gdn2 {
 namespace {
 
 const char* kNames[kNumKernels] = {"chunk_intra_kernel", "chunk_scan_fwd_kernel", "chunk_scan_bwd_kernel",
-                                   "chunk_bwd_intra_kernel", "recurrent_kernel", "cp_kernel"};
+                                   "chunk_bwd_intra_kernel", "recurrent_kernel", "cp_kernel",
+                                   "chunk_scan_fwd_tc_kernel"};
 
 struct Pending {
   int id;

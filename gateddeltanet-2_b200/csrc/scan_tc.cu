@@ -1,0 +1,479 @@
+// Forward state scan on 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// for d_k = d_v = 128: chunk_gated_delta_rule_fwd_h with its fused output
+// (reference: lit_gpt/gdn2_ops/chunk_kda.py:983-1335, called from
+// chunk_gdn2.py:1205-1359), restated in transposed form so that every
+// product has M = 128 (the state's V rows):
+//
+//     v_new^T = U^T - S^T Y^T                  (MMA1: S^T Y^T,   N = 64, K = 128)
+//     o^T     = scale S^T qg^T + v_new^T Aqk^T (MMA2 / MMA3,     N = 64, K = 128 / 64)
+//     S^T    <- S^T Diag(2^G_last) + v_new^T kg(MMA4,            N = 128, K = 64)
+//
+// One CTA per (sequence, head).  S^T lives in TMEM for the whole sequence
+// (lane v = state column v, TMEM column k = state row k, fp32); the products
+// accumulate in TMEM; operands sit in shared memory in the 128-byte swizzled
+// layout TMA writes.  MMA1 and MMA2 share A = S^T and run as one N = 128
+// product over the stacked [Y; qg] tile.  Warp roles:
+//   warps 0-7  state warps: TMEM lane quarter w % 4, column half w / 4.  Per
+//              chunk they turn S^T into the bf16 operand (and the saved chunk
+//              state h), apply the decay in TMEM, form v_new from MMA1 and U
+//              (in place over the U tile) and o (into a [t][v] tile).
+//   warp 8     allocates TMEM; lane 0 issues the MMAs and commits them.
+//   warp 9     lane 0 loads the next chunk's tiles by TMA (and G_last by a
+//              bulk copy) into the other stage.
+//   warp 10    writes the chunk state h^T (a TMA store of the bf16 S^T
+//              operand tile itself) and the v_new and o tiles: a TMA store per
+//              full chunk, 16-byte row copies for the ragged last chunk of a
+//              sequence (a tile store would run into the next sequence's rows).
+// Every wait is bounded (tc::kWaitLimitNs); a wait that gives up sets
+// g_tc_fault, abandons the scan and still frees TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "chunk_layout.cuh"
+#include "common.cuh"
+#include "profile.cuh"
+#include "tc.cuh"
+
+namespace gdn2 {
+
+__device__ unsigned int g_tc_fault;  // bit 0: a bounded wait in a tcgen05 kernel gave up
+
+namespace {
+
+constexpr int kTcK = 128, kTcV = 128;
+constexpr int kStateThreads = 256;
+constexpr int kTcThreads = kStateThreads + 96;
+constexpr int kWarpMma = 8, kWarpLoad = 9, kWarpStore = 10;
+constexpr uint32_t kTileBytes = 64 * 64 * 2;  // one [64 x 64] bf16 swizzled tile
+constexpr uint32_t kStageTx = 9 * kTileBytes + kTcK * 4;
+
+// TMEM columns (fp32, 128 lanes)
+constexpr uint32_t kColS = 0;      // S^T            [128 x 128]
+constexpr uint32_t kColAV = 128;   // S^T Y^T        [128 x 64]  } one N = 128 product
+constexpr uint32_t kColAO1 = 192;  // S^T qg^T       [128 x 64]  }
+constexpr uint32_t kColAO2 = 256;  // v_new^T Aqk^T  [128 x 64]
+constexpr uint32_t kTmemCols = 512;
+
+struct alignas(1024) TcStage {
+  __nv_bfloat16 YQ[2][128 * 64];  // per 64-column block of k: rows 0-63 Y, rows 64-127 qg
+  __nv_bfloat16 KG[2][64 * 64];   // [t][k]  (B operand of MMA4, N-major)
+  __nv_bfloat16 U[2][64 * 64];    // [t][v]; overwritten in place by v_new
+  __nv_bfloat16 Aqk[64 * 64];     // [t][s]
+  float glast[kTcK];              // G of the chunk's last token (log2 units)
+};
+
+struct alignas(1024) TcSmem {
+  TcStage st[2];
+  __nv_bfloat16 SA[2][128 * 64];  // S^T in bf16, [v][k], two 64-column blocks
+  __nv_bfloat16 VN[128 * 64];     // v_new^T in bf16, [v][t]
+  __nv_bfloat16 OT[2][64 * 64];   // o in bf16, [t][v], two 64-column blocks
+  float D[kTcK];                  // 2^G_last of the current chunk
+  uint64_t full[2], empty[2];
+  uint64_t d_ready, sa_ready, sa_free, mma12, vn_ready, mma34, o_full, ot_free;
+  uint32_t tbase;
+};
+static_assert(sizeof(TcSmem) + 1024 <= 227 * 1024, "tcgen05 scan shared memory");
+static_assert(offsetof(TcStage, glast) % 16 == 0, "bulk copy target alignment");
+
+GDN2_DEV uint64_t kdesc(const void* p, uint32_t byte_off) {
+  return tc::sdesc_sw128(tc::smem_u32(p) + byte_off, 16, 1024);
+}
+
+GDN2_DEV void fault() { atomicOr(&g_tc_fault, 1u); }
+
+// Bounded wait whose outcome is the same on every lane of the warp (the
+// warp-collective TMEM loads and stores after it must not diverge).
+GDN2_DEV bool warp_wait(uint64_t* bar, uint32_t parity) {
+  const bool r = tc::mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, r);
+}
+
+GDN2_DEV uint4 pack8(const float* x) {
+  uint4 pk;
+  pk.x = pack_bf16(x[0], x[1]);
+  pk.y = pack_bf16(x[2], x[3]);
+  pk.z = pack_bf16(x[4], x[5]);
+  pk.w = pack_bf16(x[6], x[7]);
+  return pk;
+}
+
+// rows [0, L) of a [64 x 128] bf16 tile (two swizzled 64-column blocks) to
+// global [tokens, H, 128] at token t0, head h; one warp, 16-byte pieces
+GDN2_DEV void copy_rows_out(const __nv_bfloat16 (*tile)[64 * 64], __nv_bfloat16* dst, int64_t t0, int64_t H,
+                            int64_t h, int L, int lane) {
+  for (int i = lane; i < L * 16; i += 32) {
+    const int t = i >> 4, piece = i & 15, b = piece >> 3, p = piece & 7;
+    const uint4 val = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(tile[b]) + t * 128 +
+                                                       ((p ^ (t & 7)) << 4));
+    *reinterpret_cast<uint4*>(dst + ((t0 + t) * H + h) * 128 + piece * 8) = val;
+  }
+}
+
+template <bool kSave>
+__global__ void __launch_bounds__(kTcThreads, 1)
+chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid_constant__ CUtensorMap tmY,
+                         const __grid_constant__ CUtensorMap tmQG, const __grid_constant__ CUtensorMap tmKG,
+                         const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmVN,
+                         const __grid_constant__ CUtensorMap tmH) {
+  extern __shared__ unsigned char smem_raw[];
+  TcSmem& sm = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t H = a.H;
+  const int64_t n = blockIdx.x / H, h = blockIdx.x % H;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t bos, len;
+  geo.seq(n, bos, len);
+  const int nchunks = (int)((len + kChunk - 1) / kChunk);
+  const int64_t c0 = geo.chunk0(n);
+  auto chunk_len = [&](int c) {
+    const int64_t r = len - (int64_t)c * kChunk;
+    return (int)(r < kChunk ? r : kChunk);
+  };
+
+  if (tid == 0) {
+    tc::mbar_init(&sm.full[0], 1);
+    tc::mbar_init(&sm.full[1], 1);
+    tc::mbar_init(&sm.empty[0], 2);  // the MMAs' commit + the v_new store having read U
+    tc::mbar_init(&sm.empty[1], 2);
+    tc::mbar_init(&sm.d_ready, kStateThreads);
+    tc::mbar_init(&sm.sa_ready, kStateThreads);
+    tc::mbar_init(&sm.sa_free, 1);
+    tc::mbar_init(&sm.mma12, 1);
+    tc::mbar_init(&sm.vn_ready, kStateThreads);
+    tc::mbar_init(&sm.mma34, 1);
+    tc::mbar_init(&sm.o_full, kStateThreads);
+    tc::mbar_init(&sm.ot_free, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == kWarpMma) tc::tmem_alloc(&sm.tbase, kTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tb = sm.tbase;
+  bool ok = true;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ state warps
+    const int qtr = warp & 3, half = warp >> 2;
+    const int v = 32 * qtr + lane;
+    const uint32_t tl = tb + ((uint32_t)(32 * qtr) << 16);
+    const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
+    const int kb0 = 64 * half;  // this thread's state rows k (step 1, final state)
+    const int tb0 = 32 * half;  // this thread's tokens t (v_new, o)
+    {
+      const float* h0 = (a.flags & GDN2_HAS_H0) ? a.h0 + (n * H + h) * (int64_t)kTcK * kTcV : nullptr;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int k = kb0 + 32 * j + i;
+          x[i] = h0 ? (tr ? h0[(int64_t)v * kTcK + k] : h0[(int64_t)k * kTcV + v]) : 0.f;
+        }
+        tc::tmem_st32(tl + kColS + kb0 + 32 * j, x);
+      }
+      tc::tmem_wait_st();
+    }
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c & 1;
+      TcStage& st = sm.st[s];
+      const int L = chunk_len(c);
+      if (!(ok = warp_wait(&sm.full[s], (c >> 1) & 1))) break;
+      if (half == 0) sm.D[v] = exp2_approx(st.glast[v]);
+      tc::mbar_arrive(&sm.d_ready);
+      if (!(ok = warp_wait(&sm.d_ready, c & 1))) break;
+
+      // step 1: entering state -> bf16 operand rows (also the saved h^T); decay in TMEM
+      if (kSave && c > 0 && !(ok = warp_wait(&sm.sa_free, (c - 1) & 1))) break;
+      char* sarow = reinterpret_cast<char*>(sm.SA[half]) + v * 128;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[32];
+        tc::tmem_ld32(tl + kColS + kb0 + 32 * j, x);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(sarow + (((4 * j + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0 + 32 * j);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 d = d4[q];
+          x[4 * q + 0] *= d.x;
+          x[4 * q + 1] *= d.y;
+          x[4 * q + 2] *= d.z;
+          x[4 * q + 3] *= d.w;
+        }
+        tc::tmem_st32(tl + kColS + kb0 + 32 * j, x);
+      }
+      tc::tmem_wait_st();
+      tc::fence_proxy_async();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.sa_ready);
+
+      // step 2: v_new = U - (S^T Y^T)^T, in place over U and as the MMA operand
+      if (!(ok = warp_wait(&sm.mma12, c & 1))) break;
+      tc::tc_fence_after();
+      {
+        float x[32];
+        tc::tmem_ld32(tl + kColAV + tb0, x);
+        tc::tmem_wait_ld();
+        char* ut = reinterpret_cast<char*>(st.U[v >> 6]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = tb0 + i;
+          __nv_bfloat16* up = reinterpret_cast<__nv_bfloat16*>(ut + tc::sw128_off(t, v & 63));
+          const __nv_bfloat16 vn = __float2bfloat16_rn(t < L ? __bfloat162float(*up) - x[i] : 0.f);
+          if (kSave) *up = vn;
+          x[i] = __bfloat162float(vn);
+        }
+        char* row = reinterpret_cast<char*>(sm.VN) + v * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+      }
+      tc::fence_proxy_async();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.vn_ready);
+
+      // step 3: o = scale qg S + Aqk v_new, into the [t][v] tile
+      if (!(ok = warp_wait(&sm.mma34, c & 1))) break;
+      tc::tc_fence_after();
+      {
+        float x1[32], x2[32];
+        tc::tmem_ld32(tl + kColAO1 + tb0, x1);
+        tc::tmem_ld32(tl + kColAO2 + tb0, x2);
+        tc::tmem_wait_ld();
+        if (c > 0 && !(ok = warp_wait(&sm.ot_free, (c - 1) & 1))) break;
+        char* ot = reinterpret_cast<char*>(sm.OT[v >> 6]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          *reinterpret_cast<__nv_bfloat16*>(ot + tc::sw128_off(tb0 + i, v & 63)) =
+              __float2bfloat16_rn(fmaf(a.scale, x1[i], x2[i]));
+      }
+      tc::fence_proxy_async();
+      tc::mbar_arrive(&sm.o_full);
+    }
+    if (ok && (a.flags & GDN2_STORE_FINAL)) {
+      float* ht = a.ht + (n * H + h) * (int64_t)kTcK * kTcV;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[32];
+        tc::tmem_ld32(tl + kColS + kb0 + 32 * j, x);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int k = kb0 + 32 * j + i;
+          if (tr) ht[(int64_t)v * kTcK + k] = x[i];
+          else ht[(int64_t)k * kTcV + v] = x[i];
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nchunks > 0) {
+      constexpr uint32_t kId64 = tc::idesc_bf16(128, 64, 0, 0);
+      constexpr uint32_t kId128 = tc::idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t kIdS = tc::idesc_bf16(128, 128, 0, 1);
+      uint64_t* last = nullptr;  // barrier of the last commit and its phase parity
+      uint32_t last_par = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c & 1;
+        TcStage& st = sm.st[s];
+        if (!(ok = tc::mbar_wait(&sm.full[s], (c >> 1) & 1) && tc::mbar_wait(&sm.sa_ready, c & 1))) break;
+        tc::tc_fence_after();
+        // [S^T Y^T | S^T qg^T] = S^T [Y; qg]^T
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::mma_bf16(tb + kColAV, kdesc(sm.SA[kk >> 2], (kk & 3) * 32), kdesc(st.YQ[kk >> 2], (kk & 3) * 32),
+                       kId128, kk > 0);
+        tc::mma_commit(&sm.mma12);
+        last = &sm.mma12;
+        last_par = c & 1;
+        if (!(ok = tc::mbar_wait(&sm.vn_ready, c & 1))) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + kColAO2, kdesc(sm.VN, kk * 32), kdesc(st.Aqk, kk * 32), kId64, kk > 0);
+        // kg as an N-major operand: 64-column blocks 8 KB apart, 8-row groups 1 KB apart
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + kColS, kdesc(sm.VN, kk * 32),
+                       tc::sdesc_sw128(tc::smem_u32(st.KG[0]) + kk * 2048, kTileBytes, 1024), kIdS, 1);
+        tc::mma_commit(&sm.mma34);
+        tc::mma_commit(&sm.empty[s]);
+        last = &sm.mma34;
+        last_par = c & 1;
+      }
+      // the MMAs issued have completed before TMEM is released
+      if (last && !tc::mbar_wait(last, last_par)) ok = false;
+    }
+  } else if (warp == kWarpLoad) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tc::prefetch_tensormap(&tmY);
+      tc::prefetch_tensormap(&tmQG);
+      tc::prefetch_tensormap(&tmKG);
+      tc::prefetch_tensormap(&tmU);
+      tc::prefetch_tensormap(&tmA);
+      int c = 0;
+      for (; c < nchunks; ++c) {
+        const int s = c & 1;
+        TcStage& st = sm.st[s];
+        if (c >= 2 && !(ok = tc::mbar_wait(&sm.empty[s], ((c >> 1) - 1) & 1))) break;
+        const int64_t t0 = bos + (int64_t)c * kChunk;
+        const int L = chunk_len(c);
+        const int tt = (int)t0, hh = (int)h;
+        tc::mbar_arrive_expect_tx(&sm.full[s], kStageTx);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          tc::tma_load_3d(st.YQ[b], &tmY, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.YQ[b] + 64 * 64, &tmQG, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.KG[b], &tmKG, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.U[b], &tmU, &sm.full[s], 64 * b, hh, tt);
+        }
+        tc::tma_load_3d(st.Aqk, &tmA, &sm.full[s], 0, hh, tt);
+        tc::bulk_load(st.glast, ws.G + ((t0 + L - 1) * H + h) * kTcK, kTcK * 4, &sm.full[s]);
+      }
+      // loads in flight land before the CTA exits
+      for (int j = (c < 2 ? 0 : c - 2); j < c; ++j)
+        if (!tc::mbar_wait(&sm.full[j & 1], (j >> 1) & 1)) ok = false;
+    }
+  } else {
+    // ------------------------------------------------------------ output writer
+    // The state warps cannot run more than one phase of sa_ready or o_full
+    // ahead of this warp (they wait for sa_free before the next operand tile
+    // and for ot_free before the next o tile); o_full follows their in-place
+    // v_new writes of the same chunk.
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.o);
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c & 1;
+      TcStage& st = sm.st[s];
+      const int64_t t0 = bos + (int64_t)c * kChunk;
+      const int L = chunk_len(c);
+      if (kSave) {
+        // h^T of this chunk straight out of the S^T operand tile
+        if (!(ok = warp_wait(&sm.sa_ready, c & 1))) break;
+        if (lane == 0) {
+          const int row = (int)(((c0 + c) * H + h) * kTcV);
+          tc::tma_store_2d(&tmH, sm.SA[0], 0, row);
+          tc::tma_store_2d(&tmH, sm.SA[1], 64, row);
+          tc::bulk_commit();
+          tc::bulk_wait_read_all();
+          tc::mbar_arrive(&sm.sa_free);
+        }
+        __syncwarp();
+      }
+      if (!(ok = warp_wait(&sm.o_full, c & 1))) break;
+      if (L == kChunk) {
+        if (lane == 0) {
+          if (kSave) {
+            tc::tma_store_3d(&tmVN, st.U[0], 0, (int)h, (int)t0);
+            tc::tma_store_3d(&tmVN, st.U[1], 64, (int)h, (int)t0);
+          }
+          tc::tma_store_3d(&tmO, sm.OT[0], 0, (int)h, (int)t0);
+          tc::tma_store_3d(&tmO, sm.OT[1], 64, (int)h, (int)t0);
+          tc::bulk_commit();
+          tc::bulk_wait_read_all();
+        }
+      } else {
+        if (kSave) copy_rows_out(st.U, ws.v_new, t0, H, h, L, lane);
+        copy_rows_out(sm.OT, o, t0, H, h, L, lane);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&sm.empty[s]);
+        tc::mbar_arrive(&sm.ot_free);
+      }
+    }
+    if (lane == 0) tc::bulk_wait_all();
+  }
+
+  if (!ok) fault();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tb, kTmemCols);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// [tokens, H, inner] bf16 -> tiles of 64 tokens x 64 inner of one head, swizzled 128 B
+bool token_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t H, uint64_t tokens) {
+  auto enc = encode_fn();
+  if (!enc || !base) return false;
+  cuuint64_t dims[3] = {inner, H, tokens};
+  cuuint64_t strides[2] = {inner * 2, H * inner * 2};
+  cuuint32_t box[3] = {64, 1, 64};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [rows, inner] bf16 -> tiles of 128 rows x 64 inner, swizzled 128 B
+bool rows_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows) {
+  auto enc = encode_fn();
+  if (!enc || !base) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool scan_fwd_tc_supported(const gdn2_chunk_args& a) { return a.K == kTcK && a.V == kTcV; }
+
+int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
+  const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T, H = (uint64_t)a.H;
+  const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  CUtensorMap mY, mQG, mKG, mU, mA, mO, mVN, mH;
+  if (!token_map(&mY, ws.Y, kTcK, H, tokens) || !token_map(&mQG, ws.qg, kTcK, H, tokens) ||
+      !token_map(&mKG, ws.kg, kTcK, H, tokens) || !token_map(&mU, ws.U, kTcV, H, tokens) ||
+      !token_map(&mA, ws.Aqk, kChunk, H, tokens) || !token_map(&mO, a.o, kTcV, H, tokens))
+    return GDN2_ERR_TENSOR_MAP;
+  if (save ? !token_map(&mVN, ws.v_new, kTcV, H, tokens) ||
+                 !rows_map(&mH, ws.h, kTcK, (uint64_t)a.NT * H * kTcV)
+           : false)
+    return GDN2_ERR_TENSOR_MAP;
+  if (!save) mVN = mH = mO;  // unused without SAVE_FOR_BWD
+  auto kern = save ? chunk_scan_fwd_tc_kernel<true> : chunk_scan_fwd_tc_kernel<false>;
+  const int smem = (int)sizeof(TcSmem) + 1024;
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  ProfScope ps(kKScanFwdTc, s);
+  kern<<<(unsigned)(a.N * a.H), kTcThreads, smem, s>>>(a, ws, mY, mQG, mKG, mU, mA, mO, mVN, mH);
+  GDN2_LAUNCH_CHECK();
+  return 0;
+}
+
+// Reads (and optionally clears) the fault word of the current device.
+int tc_fault_read(int clear, unsigned int* out) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_fault, sizeof(v));
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  if (clear && v) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_tc_fault, &z, sizeof(z));
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  *out = v;
+  return 0;
+}
+
+}  // namespace gdn2

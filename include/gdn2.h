@@ -67,7 +67,8 @@ enum gdn2_status {
   GDN2_ERR_WORKSPACE = 6,       /* workspace pointer NULL or too small */
   GDN2_ERR_FLAGS = 7,
   GDN2_ERR_NO_DEVICE = 8,
-  GDN2_ERR_SCRATCH_LIMIT = 9    /* problem larger than gdn2_chunk_fwd_static_scratch's 32 MiB */
+  GDN2_ERR_SCRATCH_LIMIT = 9,   /* problem larger than gdn2_chunk_fwd_static_scratch's 32 MiB */
+  GDN2_ERR_TENSOR_MAP = 10      /* the driver could not describe a workspace array for TMA */
 };
 
 /* ------------------------------------------------------------------------- */
@@ -235,6 +236,13 @@ typedef struct gdn2_kernel_stat {
 } gdn2_kernel_stat;
 int gdn2_profile_enable(int on);
 int gdn2_profile_read(gdn2_kernel_stat* out, int max_entries);
+
+/* Fault word of the current device (no reference counterpart).  The
+ * tensor-core kernels bound every wait on a barrier; a wait that gives up
+ * abandons its work, sets bit 0 of this word and returns, leaving the context
+ * usable.  Writes the word to *out (after a device sync the caller performs)
+ * and clears it when clear != 0.  Returns 0 or a negative CUDA error. */
+int gdn2_device_fault_read(int clear, unsigned int* out);
 
 /* ------------------------------------------------------------------------- */
 const char* gdn2_status_string(int status);
