@@ -187,24 +187,31 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       // step 1: entering state -> bf16 operand rows (also the saved h^T); decay in TMEM
       if (kSave && c > 0 && !(ok = warp_wait(&sm.sa_free, (c - 1) & 1))) break;
       char* sarow = reinterpret_cast<char*>(sm.SA[half]) + v * 128;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float x[32];
-        tc::tmem_ld32(tl + kColS + kb0 + 32 * j, x);
+      {
+        float x0[32], x1[32];
+        tc::tmem_ld32(tl + kColS + kb0, x0);
+        tc::tmem_ld32(tl + kColS + kb0 + 32, x1);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(sarow + (((4 * j + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
-        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0 + 32 * j);
+        for (int q = 0; q < 4; ++q) {
+          *reinterpret_cast<uint4*>(sarow + ((q ^ (v & 7)) << 4)) = pack8(x0 + 8 * q);
+          *reinterpret_cast<uint4*>(sarow + (((4 + q) ^ (v & 7)) << 4)) = pack8(x1 + 8 * q);
+        }
+        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float4 d = d4[q];
-          x[4 * q + 0] *= d.x;
-          x[4 * q + 1] *= d.y;
-          x[4 * q + 2] *= d.z;
-          x[4 * q + 3] *= d.w;
+          const float4 d = d4[q], e = d4[8 + q];
+          x0[4 * q + 0] *= d.x;
+          x0[4 * q + 1] *= d.y;
+          x0[4 * q + 2] *= d.z;
+          x0[4 * q + 3] *= d.w;
+          x1[4 * q + 0] *= e.x;
+          x1[4 * q + 1] *= e.y;
+          x1[4 * q + 2] *= e.z;
+          x1[4 * q + 3] *= e.w;
         }
-        tc::tmem_st32(tl + kColS + kb0 + 32 * j, x);
+        tc::tmem_st32(tl + kColS + kb0, x0);
+        tc::tmem_st32(tl + kColS + kb0 + 32, x1);
       }
       tc::tmem_wait_st();
       tc::fence_proxy_async();
@@ -215,17 +222,31 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       if (!(ok = warp_wait(&sm.mma12, c & 1))) break;
       tc::tc_fence_after();
       {
+        // this thread's U column (32 tokens), read while the TMEM load is in flight
         float x[32];
         tc::tmem_ld32(tl + kColAV + tb0, x);
-        tc::tmem_wait_ld();
-        char* ut = reinterpret_cast<char*>(st.U[v >> 6]);
+        __nv_bfloat16* ucol = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(st.U[v >> 6]) +
+                                                            ((v & 7) << 1));
+        const int vb = (v & 63) >> 3;
+        __nv_bfloat16 u[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int t = tb0 + i;
-          __nv_bfloat16* up = reinterpret_cast<__nv_bfloat16*>(ut + tc::sw128_off(t, v & 63));
-          const __nv_bfloat16 vn = __float2bfloat16_rn(t < L ? __bfloat162float(*up) - x[i] : 0.f);
-          if (kSave) *up = vn;
+          u[i] = ucol[(t * 128 + ((vb ^ (t & 7)) << 4)) >> 1];
+        }
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const __nv_bfloat16 vn = __float2bfloat16_rn(tb0 + i < L ? __bfloat162float(u[i]) - x[i] : 0.f);
+          u[i] = vn;
           x[i] = __bfloat162float(vn);
+        }
+        if (kSave) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = tb0 + i;
+            ucol[(t * 128 + ((vb ^ (t & 7)) << 4)) >> 1] = u[i];
+          }
         }
         char* row = reinterpret_cast<char*>(sm.VN) + v * 128;
 #pragma unroll

@@ -62,14 +62,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// The waiting thread is suspended in hardware until the phase completes or
+// the hint (ns) runs out, so waiting warps take no issue slots from the rest.
+constexpr uint32_t kSuspendHintNs = 10000000u;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(addr), "r"(parity)
+      : "r"(addr), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
