@@ -68,10 +68,12 @@ struct IntraSmem {
     } s;
     struct {
       alignas(16) __nv_bfloat16 KB2G[kChunk][LK];
+      alignas(16) __nv_bfloat16 YS[kChunk][LK];  // Y, staged for 16-byte stores
+      alignas(16) __nv_bfloat16 US[kChunk][LV];  // U, staged for 16-byte stores
     } w;
   } u;
   alignas(16) __nv_bfloat16 WV[kChunk][LV];  // w * v, formed right after the loads
-  alignas(16) float P[4][16][17];        // solve scratch
+  alignas(16) float P[4][16][16];        // solve scratch
   alignas(16) float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
   alignas(16) uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
   int nflag[4];
@@ -143,22 +145,33 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     }
   }
   cp_async_commit();
-  // each thread's b values for steps 3 and 7 (element i = tid + 256 u), issued now
-  constexpr int kBPerThread = kChunk * K / kIntraThreads;
-  float breg[kBPerThread];
+  // each thread's b values for steps 3 and 7, issued now: vectors g = tid + 256 u
+  // of 8 consecutive channels (row g / (K/8), channels from 8 (g % (K/8)))
+  constexpr int kVec = kChunk * K / 8 / kIntraThreads;
+  float breg[kVec][8];
 #pragma unroll
-  for (int u = 0; u < kBPerThread; ++u) {
-    const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
-    breg[u] = r < L ? ld_bw<TB>(a.b, ((t0 + r) * H + h) * K + c) : 0.f;
+  for (int u = 0; u < kVec; ++u) {
+    const int g = tid + u * kIntraThreads, r = g / (K / 8), c0 = (g % (K / 8)) * 8;
+    if (r < L) {
+      ld8(static_cast<const TB*>(a.b) + ((t0 + r) * H + h) * K + c0, breg[u]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) breg[u][e] = 0.f;
+    }
   }
   cp_async_wait<0>();
   __syncthreads();
   {
     const TB* wst = reinterpret_cast<const TB*>(&sm.Aqk[0][0]);
     const __nv_bfloat16* vst = reinterpret_cast<const __nv_bfloat16*>(&sm.Af[0][0]);
-    for (int i = tid; i < kChunk * V; i += kIntraThreads) {
-      const int r = i / V, c = i % V;
-      sm.WV[r][c] = __float2bfloat16_rn(to_f(wst[r * V + c]) * __bfloat162float(vst[r * V + c]));
+    for (int g = tid; g < kChunk * V / 8; g += kIntraThreads) {
+      const int r = g / (V / 8), c0 = (g % (V / 8)) * 8;
+      float w8[8], v8[8];
+      ld8(wst + r * V + c0, w8);
+      ld8(vst + r * V + c0, v8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w8[e] *= v8[e];
+      st8(&sm.WV[r][c0], w8);
     }
   }
   if (l2) {
@@ -195,11 +208,15 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   // ---- 2. gate activation + chunk-local cumsum (log2 units), in smem --------
   const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
   const bool lbnd = a.flags & GDN2_LOWER_BOUND;
-  for (int c = tid; c < K; c += kIntraThreads) {
+  {
+    // every thread: channel c, rows [r0, r0 + kRows); the parts' totals are
+    // exchanged through Dblk (free until step 3)
+    constexpr int kParts = kIntraThreads / K, kRows = kChunk / kParts;
+    const int c = tid % K, part = tid / K, r0 = part * kRows;
     const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
     const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
     float Gc = 0.f;
-    for (int r = 0; r < kChunk; ++r) {
+    for (int r = r0; r < r0 + kRows; ++r) {
       float x = sm.G[r][c];
       if (gate) {
         x += bias;
@@ -207,6 +224,13 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       }
       if (r < L) Gc += x * kRcpLn2;
       sm.G[r][c] = Gc;  // padded rows repeat G_last
+    }
+    sm.Dblk[part][c] = Gc;
+    __syncthreads();
+    if (part > 0) {
+      float off = 0.f;
+      for (int q = 0; q < part; ++q) off += sm.Dblk[q][c];
+      for (int r = r0; r < r0 + kRows; ++r) sm.G[r][c] += off;
     }
   }
   __syncthreads();
@@ -240,24 +264,43 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   }
   {
 #pragma unroll
-    for (int u = 0; u < kBPerThread; ++u) {
-      const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
+    for (int u = 0; u < kVec; ++u) {
+      const int g = tid + u * kIntraThreads, r = g / (K / 8), c0 = (g % (K / 8)) * 8;
       const int blk = r >> 4, a0 = blk * 16;
-      const float kq = __bfloat162float(sm.Kt[r][c]);
-      const float qq = __bfloat162float(sm.Q[r][c]);
-      const float bb = breg[u];
-      const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);  // <= 1
-      sm.u.s.QG[r][c] = __float2bfloat16_rn(qq * rowf);
-      sm.u.s.KBG[r][c] = __float2bfloat16_rn(bb * kq * rowf);
-      // column operands for every anchor at or after this row's block
-      const bool fl = sm.flag[blk][c];
-      const float fd = fl ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);  // >= 1, bounded
-      sm.u.s.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kq * fd);
+      float kq[8], qq[8], Gr[8], Ga[8], o1[8], o2[8], o3[8];
+      ld8(&sm.Kt[r][c0], kq);
+      ld8(&sm.Q[r][c0], qq);
+      ld8(&sm.G[r][c0], Gr);
+      ld8(&sm.G[a0][c0], Ga);
+      const uint2 fl2 = *reinterpret_cast<const uint2*>(&sm.flag[blk][c0]);
+      const uint8_t* fl = reinterpret_cast<const uint8_t*>(&fl2);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float rowf = exp2_approx(Gr[e] - Ga[e]);  // <= 1
+        o1[e] = qq[e] * rowf;
+        o2[e] = breg[u][e] * kq[e] * rowf;
+        // column operand of this row's own anchor: >= 1, bounded unless flagged
+        o3[e] = kq[e] * (fl[e] ? 0.f : exp2_approx(Ga[e] - Gr[e]));
+      }
+      st8(&sm.u.s.QG[r][c0], o1);
+      st8(&sm.u.s.KBG[r][c0], o2);
+      st8(&sm.u.s.KN[anchor_row0(blk) + r][c0], o3);
+      // column operands for every later anchor (<= 1)
       if (blk < 3) {
-        float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);  // <= 1
+        float f[8];
+        ld8(&sm.G[a0 + 16][c0], Ga);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = exp2_approx(Ga[e] - Gr[e]);
         for (int ai = blk + 1; ai < 4; ++ai) {
-          if (ai > blk + 1) f *= sm.Dblk[ai][c];
-          sm.u.s.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kq * f);
+          if (ai > blk + 1) {
+            float d[8];
+            ld8(&sm.Dblk[ai][c0], d);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] *= d[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o3[e] = kq[e] * f[e];
+          st8(&sm.u.s.KN[anchor_row0(ai) + r][c0], o3);
         }
       }
     }
@@ -342,66 +385,98 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     for (int r = 0; r < 16; ++r) sm.Af[o + r][o + j] = x[r];
   }
   __syncthreads();
-  // 6b: off-diagonal blocks by increasing distance d = i - j
+  // 6b: off-diagonal blocks by increasing distance d = i - j; a thread owns one
+  //     row and 4 consecutive columns of a block
   for (int d = 1; d < 4; ++d) {
     const int nb = 4 - d;
     // P_j = sum_{m=j}^{i-1} T_im A_mj for each block (j+d, j)
-    for (int e = tid; e < nb * 256; e += kIntraThreads) {
-      const int jb = e / 256, rc = e % 256, r = rc / 16, c = rc % 16;
+    for (int e = tid; e < nb * 64; e += kIntraThreads) {
+      const int jb = e / 64, r = (e % 64) / 4, c4 = (e % 4) * 4;
       const int ib = jb + d;
-      float acc = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int m = jb; m < ib; ++m)
 #pragma unroll
-        for (int x = 0; x < 16; ++x) acc += sm.Tm[ib * 16 + r][m * 16 + x] * sm.Af[m * 16 + x][jb * 16 + c];
-      sm.P[jb][r][c] = acc;
+        for (int x = 0; x < 16; ++x) {
+          const float t = sm.Tm[ib * 16 + r][m * 16 + x];
+          const float4 av = *reinterpret_cast<const float4*>(&sm.Af[m * 16 + x][jb * 16 + c4]);
+          acc.x += t * av.x;
+          acc.y += t * av.y;
+          acc.z += t * av.z;
+          acc.w += t * av.w;
+        }
+      *reinterpret_cast<float4*>(&sm.P[jb][r][c4]) = acc;
     }
     __syncthreads();
-    for (int e = tid; e < nb * 256; e += kIntraThreads) {
-      const int jb = e / 256, rc = e % 256, r = rc / 16, c = rc % 16;
+    for (int e = tid; e < nb * 64; e += kIntraThreads) {
+      const int jb = e / 64, r = (e % 64) / 4, c4 = (e % 4) * 4;
       const int ib = jb + d;
-      float acc = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int x = 0; x < 16; ++x) acc += sm.Af[ib * 16 + r][ib * 16 + x] * sm.P[jb][x][c];
-      sm.Af[ib * 16 + r][jb * 16 + c] = -acc;
+      for (int x = 0; x < 16; ++x) {
+        const float t = sm.Af[ib * 16 + r][ib * 16 + x];
+        const float4 pv = *reinterpret_cast<const float4*>(&sm.P[jb][x][c4]);
+        acc.x += t * pv.x;
+        acc.y += t * pv.y;
+        acc.z += t * pv.z;
+        acc.w += t * pv.w;
+      }
+      *reinterpret_cast<float4*>(&sm.Af[ib * 16 + r][jb * 16 + c4]) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
     }
     __syncthreads();
   }
   // upper blocks of A are zero; bf16 copy; Aqk / A to global
-  for (int i = tid; i < kChunk * kChunk; i += kIntraThreads) {
-    const int r = i / kChunk, s = i % kChunk;
-    const float av = s > r ? 0.f : ((r < L || s == r) ? sm.Af[r][s] : 0.f);
-    const __nv_bfloat16 ab = __float2bfloat16_rn(av);
-    sm.Ab[r][s] = ab;
+  for (int g = tid; g < kChunk * kChunk / 8; g += kIntraThreads) {
+    const int r = g / 8, s0 = (g % 8) * 8;
+    float av[8], aq[8];
+    ld8(&sm.Af[r][s0], av);
+    ld8(&sm.Aqk[r][s0], aq);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int s = s0 + e;
+      av[e] = s > r ? 0.f : ((r < L || s == r) ? av[e] : 0.f);
+    }
+    const uint4 pk = pack8(av);
+    *reinterpret_cast<uint4*>(&sm.Ab[r][s0]) = pk;
     if (r < L) {
-      const int64_t gi = ((t0 + r) * H + h) * kChunk + s;
-      ws.Akk[gi] = ab;
-      ws.Aqk[gi] = __float2bfloat16_rn(sm.Aqk[r][s]);
+      const int64_t gi = ((t0 + r) * H + h) * kChunk + s0;
+      *reinterpret_cast<uint4*>(ws.Akk + gi) = pk;
+      st8(ws.Aqk + gi, aq);
     }
   }
   // WY operands (the score operands are dead now)
   __syncthreads();
   {
 #pragma unroll
-    for (int u = 0; u < kBPerThread; ++u) {
-      const int i = tid + u * kIntraThreads, r = i / K, c = i % K;
-      const float kq = __bfloat162float(sm.Kt[r][c]);
-      const float qq = __bfloat162float(sm.Q[r][c]);
-      const float Gr = sm.G[r][c];
-      const float e = exp2_approx(Gr);
-      sm.u.w.KB2G[r][c] = __float2bfloat16_rn(breg[u] * kq * e);
+    for (int u = 0; u < kVec; ++u) {
+      const int g = tid + u * kIntraThreads, r = g / (K / 8), c0 = (g % (K / 8)) * 8;
+      float kq[8], qq[8], Gr[8], Gl[8], o1[8], o2[8], o3[8];
+      ld8(&sm.Kt[r][c0], kq);
+      ld8(&sm.Q[r][c0], qq);
+      ld8(&sm.G[r][c0], Gr);
+      ld8(&sm.G[kChunk - 1][c0], Gl);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float ex = exp2_approx(Gr[e]);
+        o1[e] = breg[u][e] * kq[e] * ex;
+        o2[e] = kq[e] * exp2_approx(Gl[e] - Gr[e]);
+        o3[e] = qq[e] * ex;
+      }
+      st8(&sm.u.w.KB2G[r][c0], o1);
       if (r < L) {
-        const int64_t gi = ((t0 + r) * H + h) * K + c;
-        ws.kg[gi] = __float2bfloat16_rn(kq * exp2_approx(sm.G[kChunk - 1][c] - Gr));
-        ws.qg[gi] = __float2bfloat16_rn(qq * e);
+        const int64_t gi = ((t0 + r) * H + h) * K + c0;
+        st8(ws.kg + gi, o2);
+        st8(ws.qg + gi, o3);
       }
     }
   }
   __syncthreads();
 
   // ---- 7. Y = A (b k 2^G), U = A (w v) ---------------------------------------
-  // each warp: 16 rows x (K/2) cols of Y, then of U
+  // each warp: 16 rows x (K/2) cols of Y, then of U; staged in shared memory and
+  // written out with 16-byte stores
   {
     const int m0 = (warp & 3) * 16;
+    const int g = lane >> 2, tq = lane & 3;
     Smem Aop{&sm.Ab[0][0], S::LAB};
     {
       constexpr int NTc = K / 2 / 8;
@@ -409,9 +484,12 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       float acc[1][NTc][4];
       zero_acc(acc);
       warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.u.w.KB2G[0][0], S::LK}, n0, 0, kChunk, lane);
-      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
-        if (r < L) ws.Y[((t0 + r) * H + h) * K + c] = __float2bfloat16_rn(v);
-      });
+#pragma unroll
+      for (int j = 0; j < NTc; ++j) {
+        const int c = n0 + 8 * j + 2 * tq;
+        *reinterpret_cast<uint32_t*>(&sm.u.w.YS[m0 + g][c]) = pack_bf16(acc[0][j][0], acc[0][j][1]);
+        *reinterpret_cast<uint32_t*>(&sm.u.w.YS[m0 + g + 8][c]) = pack_bf16(acc[0][j][2], acc[0][j][3]);
+      }
     }
     {
       constexpr int NTc = V / 2 / 8;
@@ -419,10 +497,22 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       float acc[1][NTc][4];
       zero_acc(acc);
       warp_mma<1, NTc, false, false>(acc, Aop, m0, Smem{&sm.WV[0][0], S::LV}, n0, 0, kChunk, lane);
-      acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) {
-        if (r < L) ws.U[((t0 + r) * H + h) * V + c] = __float2bfloat16_rn(v);
-      });
+#pragma unroll
+      for (int j = 0; j < NTc; ++j) {
+        const int c = n0 + 8 * j + 2 * tq;
+        *reinterpret_cast<uint32_t*>(&sm.u.w.US[m0 + g][c]) = pack_bf16(acc[0][j][0], acc[0][j][1]);
+        *reinterpret_cast<uint32_t*>(&sm.u.w.US[m0 + g + 8][c]) = pack_bf16(acc[0][j][2], acc[0][j][3]);
+      }
     }
+  }
+  __syncthreads();
+  for (int i = tid; i < L * (K / 8); i += kIntraThreads) {
+    const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+    *reinterpret_cast<uint4*>(ws.Y + ((t0 + r) * H + h) * K + p) = *reinterpret_cast<const uint4*>(&sm.u.w.YS[r][p]);
+  }
+  for (int i = tid; i < L * (V / 8); i += kIntraThreads) {
+    const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+    *reinterpret_cast<uint4*>(ws.U + ((t0 + r) * H + h) * V + p) = *reinterpret_cast<const uint4*>(&sm.u.w.US[r][p]);
   }
 }
 

@@ -38,6 +38,36 @@ GDN2_DEV uint32_t pack_bf16(float lo, float hi) {
 }
 GDN2_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// 8 consecutive elements (16-byte aligned for bf16, 32-byte for fp32) <-> registers
+GDN2_DEV void ld8(const float* p, float* x) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+GDN2_DEV void ld8(const __nv_bfloat16* p, float* x) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    x[2 * i] = __low2float(h2);
+    x[2 * i + 1] = __high2float(h2);
+  }
+}
+GDN2_DEV uint4 pack8(const float* x) {
+  uint4 pk;
+  pk.x = pack_bf16(x[0], x[1]);
+  pk.y = pack_bf16(x[2], x[3]);
+  pk.z = pack_bf16(x[4], x[5]);
+  pk.w = pack_bf16(x[6], x[7]);
+  return pk;
+}
+GDN2_DEV void st8(__nv_bfloat16* p, const float* x) { *reinterpret_cast<uint4*>(p) = pack8(x); }
+GDN2_DEV void st8(float* p, const float* x) {
+  *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(x[4], x[5], x[6], x[7]);
+}
+
 GDN2_DEV float exp2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -88,15 +88,6 @@ GDN2_DEV bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, r);
 }
 
-GDN2_DEV uint4 pack8(const float* x) {
-  uint4 pk;
-  pk.x = pack_bf16(x[0], x[1]);
-  pk.y = pack_bf16(x[2], x[3]);
-  pk.z = pack_bf16(x[4], x[5]);
-  pk.w = pack_bf16(x[6], x[7]);
-  return pk;
-}
-
 // rows [0, L) of a [64 x 128] bf16 tile (two swizzled 64-column blocks) to
 // global [tokens, H, 128] at token t0, head h; one warp, 16-byte pieces
 GDN2_DEV void copy_rows_out(const __nv_bfloat16 (*tile)[64 * 64], __nv_bfloat16* dst, int64_t t0, int64_t H,
