@@ -422,10 +422,17 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTv; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0v + 8 * j + 2 * (lane & 3) + (e & 1);
-        wl[j][e] = r < L ? ldb<TB>(a.w, tokV(r, c)) : 0.f;
-        vl[j][e] = r < L ? __bfloat162float(vin[tokV(r, c)]) : 0.f;
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0v + 8 * j + 2 * (lane & 3);
+        float2 w2 = make_float2(0.f, 0.f), v2 = make_float2(0.f, 0.f);
+        if (r < L) {
+          w2 = ld2(static_cast<const TB*>(a.w) + tokV(r, c));
+          v2 = ld2(vin + tokV(r, c));
+        }
+        wl[j][2 * x] = w2.x;
+        wl[j][2 * x + 1] = w2.y;
+        vl[j][2 * x] = v2.x;
+        vl[j][2 * x + 1] = v2.y;
       }
     float t[1][NTv][4];
     zero_acc(t);
@@ -456,16 +463,21 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-        const float Gr = sm.G[r][c];
-        const float dqi = r < L ? dq[0][j][e] * scale * exp2_approx(Gr) : 0.f;
-        const float dki = r < L ? dk[0][j][e] * exp2_approx(Glast[c] - Gr) : 0.f;
-        dq[0][j][e] = dqi;
-        dk[0][j][e] = dki;
-        const float kk = kv(r, c);
-        dG[0][j][e] = qv(r, c) * dqi - kk * dki;
-        colsum[j][e & 1] += kk * dki;
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
+        const float2 G2 = ld2(&sm.G[r][c]), Gl2 = ld2(&Glast[c]);
+        const float2 q2 = ld2(&sg.Q[r][c]), k2 = ld2(&sg.Kk[r][c]);
+        const float Gr[2] = {G2.x, G2.y}, Gl[2] = {Gl2.x, Gl2.y}, qq[2] = {q2.x, q2.y}, kk[2] = {k2.x, k2.y};
+#pragma unroll
+        for (int y = 0; y < 2; ++y) {
+          const int e = 2 * x + y;
+          const float dqi = r < L ? dq[0][j][e] * scale * exp2_approx(Gr[y]) : 0.f;
+          const float dki = r < L ? dk[0][j][e] * exp2_approx(Gl[y] - Gr[y]) : 0.f;
+          dq[0][j][e] = dqi;
+          dk[0][j][e] = dki;
+          dG[0][j][e] = qq[y] * dqi - kk[y] * dki;
+          colsum[j][y] += kk[y] * dki;
+        }
       }
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
@@ -480,9 +492,15 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
 
   // ---- phase 2: WY factors -----------------------------------------------------
-  for (int i = tid; i < kChunk * K; i += kBIntraThreads) {
-    const int r = i / K, c = i % K;
-    p2.KB2G[r][c] = __float2bfloat16_rn(bv(r, c) * kv(r, c) * exp2_approx(sm.G[r][c]));
+  for (int g = tid; g < kChunk * K / 8; g += kBIntraThreads) {
+    const int r = g / (K / 8), c0 = (g % (K / 8)) * 8;
+    float b8[8], k8[8], G8[8];
+    ld8(&sg.Bg[r][c0], b8);
+    ld8(&sg.Kk[r][c0], k8);
+    ld8(&sm.G[r][c0], G8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b8[e] = b8[e] * k8[e] * exp2_approx(G8[e]);
+    st8(&p2.KB2G[r][c0], b8);
   }
   __syncthreads();
   {
@@ -502,14 +520,19 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
         if (r < L) {
-          const float x = t[0][j][e] * exp2_approx(sm.G[r][c]);
-          const float bb = bv(r, c), kk = kv(r, c);
-          db[0][j][e] += kk * x;
-          dk[0][j][e] += bb * x;
-          dG[0][j][e] += bb * kk * x;
+          const float2 G2 = ld2(&sm.G[r][c]), b2 = ld2(&sg.Bg[r][c]), k2 = ld2(&sg.Kk[r][c]);
+          const float Gr[2] = {G2.x, G2.y}, bb[2] = {b2.x, b2.y}, kk[2] = {k2.x, k2.y};
+#pragma unroll
+          for (int y = 0; y < 2; ++y) {
+            const int e = 2 * x + y;
+            const float xx = t[0][j][e] * exp2_approx(Gr[y]);
+            db[0][j][e] += kk[y] * xx;
+            dk[0][j][e] += bb[y] * xx;
+            dG[0][j][e] += bb[y] * kk[y] * xx;
+          }
         }
       }
   }
@@ -530,20 +553,42 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   __syncthreads();
 
   // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
-  for (int i = tid; i < kChunk * K; i += kBIntraThreads) {
-    const int r = i / K, c = i % K;
+  for (int g = tid; g < kChunk * K / 8; g += kBIntraThreads) {
+    const int r = g / (K / 8), c0 = (g % (K / 8)) * 8;
     const int blk = r >> 4, a0 = blk * 16;
-    const float kk = kv(r, c);
-    const float rowf = exp2_approx(sm.G[r][c] - sm.G[a0][c]);
-    p3.QG[r][c] = __float2bfloat16_rn(qv(r, c) * rowf);
-    p3.KBG[r][c] = __float2bfloat16_rn(bv(r, c) * kk * rowf);
-    const float fd = sm.flag[blk][c] ? 0.f : exp2_approx(sm.G[a0][c] - sm.G[r][c]);
-    p3.KN[anchor_row0(blk) + r][c] = __float2bfloat16_rn(kk * fd);
+    float k8[8], q8[8], b8[8], Gr[8], Ga[8], o1[8], o2[8], o3[8];
+    ld8(&sg.Kk[r][c0], k8);
+    ld8(&sg.Q[r][c0], q8);
+    ld8(&sg.Bg[r][c0], b8);
+    ld8(&sm.G[r][c0], Gr);
+    ld8(&sm.G[a0][c0], Ga);
+    const uint2 fl2 = *reinterpret_cast<const uint2*>(&sm.flag[blk][c0]);
+    const uint8_t* fl = reinterpret_cast<const uint8_t*>(&fl2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float rowf = exp2_approx(Gr[e] - Ga[e]);
+      o1[e] = q8[e] * rowf;
+      o2[e] = b8[e] * k8[e] * rowf;
+      o3[e] = k8[e] * (fl[e] ? 0.f : exp2_approx(Ga[e] - Gr[e]));
+    }
+    st8(&p3.QG[r][c0], o1);
+    st8(&p3.KBG[r][c0], o2);
+    st8(&p3.KN[anchor_row0(blk) + r][c0], o3);
     if (blk < 3) {
-      float f = exp2_approx(sm.G[a0 + 16][c] - sm.G[r][c]);
+      float f[8], Gp[8];
+      ld8(&sm.G[a0 + 16][c0], Ga);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = exp2_approx(Ga[e] - Gr[e]);
       for (int ai = blk + 1; ai < 4; ++ai) {
-        if (ai > blk + 1) f *= exp2_approx(sm.G[ai * 16][c] - sm.G[ai * 16 - 16][c]);
-        p3.KN[anchor_row0(ai) + r][c] = __float2bfloat16_rn(kk * f);
+        if (ai > blk + 1) {
+          ld8(&sm.G[ai * 16][c0], Ga);
+          ld8(&sm.G[ai * 16 - 16][c0], Gp);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= exp2_approx(Ga[e] - Gp[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o3[e] = k8[e] * f[e];
+        st8(&p3.KN[anchor_row0(ai) + r][c0], o3);
       }
     }
   }
@@ -559,18 +604,26 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-        const float rowf = exp2_approx(sm.G[r][c] - sm.G[m0][c]);
-        const float rr = r2[0][j][e] * rowf;
-        dq[0][j][e] += r1[0][j][e] * rowf;
-        dk[0][j][e] += rr * bv(r, c);
-        db[0][j][e] += rr * kv(r, c);
-        // the decay-gradient pieces use the very bf16 operands the MMAs read
-        // (QG = q 2^(G_r - G_a), KBG = b k 2^(G_r - G_a)), so that the row and
-        // column sides below cancel exactly when summed over the chunk.
-        dG[0][j][e] += __bfloat162float(p3.QG[r][c]) * r1[0][j][e] +
-                       __bfloat162float(p3.KBG[r][c]) * r2[0][j][e];
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
+        const float2 G2 = ld2(&sm.G[r][c]), Ga2 = ld2(&sm.G[m0][c]);
+        const float2 b2 = ld2(&sg.Bg[r][c]), k2 = ld2(&sg.Kk[r][c]);
+        const float2 qg2 = ld2(&p3.QG[r][c]), kbg2 = ld2(&p3.KBG[r][c]);
+        const float Gr[2] = {G2.x, G2.y}, Ga[2] = {Ga2.x, Ga2.y}, bb[2] = {b2.x, b2.y}, kk[2] = {k2.x, k2.y};
+        const float qg[2] = {qg2.x, qg2.y}, kbg[2] = {kbg2.x, kbg2.y};
+#pragma unroll
+        for (int y = 0; y < 2; ++y) {
+          const int e = 2 * x + y;
+          const float rowf = exp2_approx(Gr[y] - Ga[y]);
+          const float rr = r2[0][j][e] * rowf;
+          dq[0][j][e] += r1[0][j][e] * rowf;
+          dk[0][j][e] += rr * bb[y];
+          db[0][j][e] += rr * kk[y];
+          // the decay-gradient pieces use the very bf16 operands the MMAs read
+          // (QG = q 2^(G_r - G_a), KBG = b k 2^(G_r - G_a)), so that the row and
+          // column sides below cancel exactly when summed over the chunk.
+          dG[0][j][e] += qg[y] * r1[0][j][e] + kbg[y] * r2[0][j][e];
+        }
       }
   }
   // column parts: this warp's rows as columns s of block rb, rows r of blocks >= rb
@@ -584,13 +637,21 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int s = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-        float cf = exp2_approx(sm.G[ib * 16][c] - sm.G[s][c]);
-        if (ib == rb && sm.flag[rb][c]) cf = 0.f;
-        dk[0][j][e] += cc[0][j][e] * cf;
-        // KN_ib[s] = bf16(k_s 2^(G_a - G_s)): the row side's operand
-        dG[0][j][e] -= __bfloat162float(p3.KN[anchor_row0(ib) + s][c]) * cc[0][j][e];
+      for (int x = 0; x < 2; ++x) {
+        const int s = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
+        const float2 Ga2 = ld2(&sm.G[ib * 16][c]), Gs2 = ld2(&sm.G[s][c]);
+        const float2 kn2 = ld2(&p3.KN[anchor_row0(ib) + s][c]);
+        const float Ga[2] = {Ga2.x, Ga2.y}, Gs[2] = {Gs2.x, Gs2.y}, kn[2] = {kn2.x, kn2.y};
+        const bool own = ib == rb;
+#pragma unroll
+        for (int y = 0; y < 2; ++y) {
+          const int e = 2 * x + y;
+          float cf = exp2_approx(Ga[y] - Gs[y]);
+          if (own && sm.flag[rb][c + y]) cf = 0.f;
+          dk[0][j][e] += cc[0][j][e] * cf;
+          // KN_ib[s] = bf16(k_s 2^(G_a - G_s)): the row side's operand
+          dG[0][j][e] -= kn[y] * cc[0][j][e];
+        }
       }
   }
   // exact per-pair contributions of flagged (block, channel)s
@@ -630,13 +691,20 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = m0 + (lane >> 2) + (e >> 1) * 8, c = n0 + 8 * j + 2 * (lane & 3) + (e & 1);
-        float g = dG[0][j][e];
-        if (r == L - 1) g += sm.last[c];
-        sm.G[r][c] = r < L ? g : 0.f;
-        pq[e >> 1] += dq[0][j][e] * qv(r, c);
-        pk[e >> 1] += dk[0][j][e] * kv(r, c);
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
+        float g0 = dG[0][j][2 * x], g1 = dG[0][j][2 * x + 1];
+        if (r == L - 1) {
+          const float2 l2v = ld2(&sm.last[c]);
+          g0 += l2v.x;
+          g1 += l2v.y;
+        }
+        *reinterpret_cast<float2*>(&sm.G[r][c]) = r < L ? make_float2(g0, g1) : make_float2(0.f, 0.f);
+        if (l2) {
+          const float2 q2 = ld2(&sg.Q[r][c]), k2 = ld2(&sg.Kk[r][c]);
+          pq[x] += dq[0][j][2 * x] * q2.x + dq[0][j][2 * x + 1] * q2.y;
+          pk[x] += dk[0][j][2 * x] * k2.x + dk[0][j][2 * x + 1] * k2.y;
+        }
       }
     if (l2) {
 #pragma unroll

@@ -54,6 +54,11 @@ GDN2_DEV void ld8(const __nv_bfloat16* p, float* x) {
     x[2 * i + 1] = __high2float(h2);
   }
 }
+// 2 consecutive elements (8-byte aligned for fp32, 4-byte for bf16)
+GDN2_DEV float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
+GDN2_DEV float2 ld2(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
 GDN2_DEV uint4 pack8(const float* x) {
   uint4 pk;
   pk.x = pack_bf16(x[0], x[1]);
