@@ -53,6 +53,7 @@ KERNEL_BYTES_PER_TOKEN_HEAD = {
     "chunk_scan_fwd_tc_kernel": 4 * 2 * 128 + 2 * 64 + 2 * 2 * 128 + (128 * 128 * 2) // 64,
     # reads Y, qg, kg, Aqk, do; writes dh (K*V bf16 / 64 tokens) and dv_new
     "chunk_scan_bwd_kernel": 3 * 2 * 128 + 2 * 64 + 2 * 128 + (128 * 128 * 2) // 64 + 2 * 128,
+    "chunk_scan_bwd_tc_kernel": 3 * 2 * 128 + 2 * 64 + 2 * 128 + (128 * 128 * 2) // 64 + 2 * 128,
     # reads h, dh, do, v_new, dv_new, A, G, q, k, b, w, v; writes dq, dk, dv, dg, db, dw
     "chunk_bwd_intra_kernel": 2 * (128 * 128 * 2) // 64 + 3 * 2 * 128 + 2 * 64 + 4 * 128
     + 2 * 2 * 128 + 2 * 4 * 128 + 2 * 128 + 3 * 2 * 128 + 3 * 4 * 128,

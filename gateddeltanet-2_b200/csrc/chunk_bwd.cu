@@ -12,7 +12,7 @@
 // tensor-core accumulators:
 //   dh[c]  = dS                                   (cotangent of the chunk's exit state)
 //   dv_new = Aqk^T do + kg dS
-//   dS    <- 2^G_last dS + scale qg^T do - Y^T dv_new
+//   dS    <- 2^G_last dS + qg^T do - Y^T dv_new     (qg carries the output scale)
 //
 // chunk_bwd_intra_kernel (one CTA per (chunk, head)), everything else in one
 // pass with all [64 x K] accumulators (dq, dk, db, dG) in registers:
@@ -138,11 +138,16 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
     cp_commit();
     cp_wait<1>();
     __syncthreads();
-    {  // dh of this chunk, 16-byte stores out of DSb
-      __nv_bfloat16* dst = bw.dh + ((c0 + ci) * H + h) * (int64_t)K * V + v0;
-      for (int i = tid; i < K * (kBScanBV / 8); i += kBScanThreads) {
-        const int r = i / (kBScanBV / 8), p = (i % (kBScanBV / 8)) * 8;
-        *reinterpret_cast<uint4*>(dst + (int64_t)r * V + p) = *reinterpret_cast<const uint4*>(&sm.DSb[r][p]);
+    {  // dh of this chunk, transposed (dh^T [v][k]), 16-byte stores
+      __nv_bfloat16* dst = bw.dh + ((c0 + ci) * H + h) * (int64_t)K * V + (int64_t)v0 * K;
+      for (int i = tid; i < kBScanBV * (K / 8); i += kBScanThreads) {
+        const int c = i / (K / 8), p = (i % (K / 8)) * 8;
+        uint4 pk;
+        pk.x = pack_bf16(__bfloat162float(sm.DSb[p + 0][c]), __bfloat162float(sm.DSb[p + 1][c]));
+        pk.y = pack_bf16(__bfloat162float(sm.DSb[p + 2][c]), __bfloat162float(sm.DSb[p + 3][c]));
+        pk.z = pack_bf16(__bfloat162float(sm.DSb[p + 4][c]), __bfloat162float(sm.DSb[p + 5][c]));
+        pk.w = pack_bf16(__bfloat162float(sm.DSb[p + 6][c]), __bfloat162float(sm.DSb[p + 7][c]));
+        *reinterpret_cast<uint4*>(dst + (int64_t)c * K + p) = pk;
       }
     }
 
@@ -162,7 +167,7 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
       const int r = i / (kBScanBV / 8), p = (i % (kBScanBV / 8)) * 8;
       *reinterpret_cast<uint4*>(bw.dvn + ((t0 + r) * H + h) * V + v0 + p) = *reinterpret_cast<const uint4*>(&sm.DV[r][p]);
     }
-    // dS <- 2^G_last dS + scale qg^T do - Y^T dv_new
+    // dS <- 2^G_last dS + qg^T do - Y^T dv_new
     if (sown) {
       float t1[MT][NT][4], t2[MT][NT][4];
       zero_acc(t1);
@@ -182,7 +187,7 @@ chunk_scan_bwd_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs 
         for (int j = 0; j < NT; ++j)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            dS[i][j][e] = dS[i][j][e] * dec[i][e >> 1] + a.scale * t1[i][j][e] - t2[i][j][e];
+            dS[i][j][e] = dS[i][j][e] * dec[i][e >> 1] + t1[i][j][e] - t2[i][j][e];
     }
     __syncthreads();
   }
@@ -225,7 +230,7 @@ struct BIntraSmem {
     alignas(16) __nv_bfloat16 DVN[kChunk][LV];
     alignas(16) __nv_bfloat16 DY[kChunk][LK];
     alignas(16) __nv_bfloat16 HsT[V][LK];  // h^T: the chunk's entering state, [v][k]
-    alignas(16) __nv_bfloat16 DH[K][LV];
+    alignas(16) __nv_bfloat16 DHT[V][LK];  // dh^T: the chunk's exit-state cotangent, [v][k]
     alignas(16) __nv_bfloat16 DO[kChunk][LV];
     alignas(16) __nv_bfloat16 VN[kChunk][LV];
   };
@@ -317,10 +322,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     for (int i = tid; i < V * (K / 8); i += kBIntraThreads) {
       const int r = i / (K / 8), p = (i % (K / 8)) * 8;
       cp_async16b(&p1.HsT[r][p], hsrc + (int64_t)r * K + p, true);
-    }
-    for (int i = tid; i < K * (V / 8); i += kBIntraThreads) {
-      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      cp_async16b(&p1.DH[r][p], dhsrc + (int64_t)r * V + p, true);
+      cp_async16b(&p1.DHT[r][p], dhsrc + (int64_t)r * K + p, true);
     }
     for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
       const int r = i / (V / 8), p = (i % (V / 8)) * 8;
@@ -370,7 +372,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 
   // ---- phase 1: products with h, dh ------------------------------------------
   warp_mma<1, NTk, false, false>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
-  warp_mma<1, NTk, false, true>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DH[0][0], S::LV}, n0, 0, V, lane);
+  warp_mma<1, NTk, false, false>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DHT[0][0], S::LK}, n0, 0, V, lane);
   {
     float t[1][NTk][4];
     zero_acc(t);
@@ -383,7 +385,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     float s = 0.f;
     if (r < K) {
       for (int v = part * (V / 4); v < (part + 1) * (V / 4); ++v)
-        s += __bfloat162float(p1.HsT[v][r]) * __bfloat162float(p1.DH[r][v]);
+        s += __bfloat162float(p1.HsT[v][r]) * __bfloat162float(p1.DHT[v][r]);
     }
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
@@ -804,15 +806,18 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
 template <int K, int V>
 int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
                   cudaStream_t s) {
-  const size_t sm2 = sizeof(BScanSmem<K>);
-  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_bwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sm2));
-  dim3 g2((unsigned)(V / kBScanBV), (unsigned)(a.N * a.H));
-  {
+  if (scan_fwd_tc_supported(a)) {
+    const int st = scan_bwd_tc_launch(a, g, ws, bw, s);
+    if (st != 0) return st;
+  } else {
+    const size_t sm2 = sizeof(BScanSmem<K>);
+    GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_bwd_kernel<K, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm2));
+    dim3 g2((unsigned)(V / kBScanBV), (unsigned)(a.N * a.H));
     ProfScope ps(kKScanBwd, s);
     chunk_scan_bwd_kernel<K, V><<<g2, kBScanThreads, sm2, s>>>(a, g, ws, bw);
+    GDN2_LAUNCH_CHECK();
   }
-  GDN2_LAUNCH_CHECK();
   if (a.NT > 0) {
     const bool bwb = a.dtype_bw == GDN2_BF16;
     const size_t sm3 = bwb ? sizeof(BIntraSmem<K, V, __nv_bfloat16>) : sizeof(BIntraSmem<K, V, float>);

@@ -21,13 +21,14 @@
 //   - A = (I+T)^-1 in fp32 on CUDA cores: 16x16 diagonal blocks by forward
 //     substitution, off-diagonal blocks A_ij = -A_ii sum_m T_im A_mj;
 //   - Y = A (b k 2^G), U = A (w v) on tensor cores; kg = k 2^(G_last - G),
-//     qg = q 2^G (recompute_w_u_fwd_gdn2_kernel, chunk_gdn2.py:837-929).
+//     qg = scale q 2^G (recompute_w_u_fwd_gdn2_kernel, chunk_gdn2.py:837-929;
+//     the output scale rides on qg so the scans need no separate multiply).
 //
 // chunk_scan_fwd_kernel (one CTA per (sequence, head, 64-column V tile)):
 //   serial over the chunks of the sequence with the [K x 64] fp32 state in
 //   tensor-core accumulator registers (chunk_gated_delta_rule_fwd_h,
 //   chunk_kda.py:983-1335, with its fused output):
-//     v_new = U - Y S ; o = scale qg S + Aqk v_new ; S <- 2^G_last * S + kg^T v_new
+//     v_new = U - Y S ; o = qg S + Aqk v_new ; S <- 2^G_last * S + kg^T v_new
 //   The next chunk's operands are prefetched with cp.async while the current
 //   chunk computes.
 #include "common.cuh"
@@ -459,7 +460,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
         const float ex = exp2_approx(Gr[e]);
         o1[e] = breg[u][e] * kq[e] * ex;
         o2[e] = kq[e] * exp2_approx(Gl[e] - Gr[e]);
-        o3[e] = qq[e] * ex;
+        o3[e] = qq[e] * ex * a.scale;
       }
       st8(&sm.u.w.KB2G[r][c0], o1);
       if (r < L) {
@@ -665,13 +666,12 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
             *reinterpret_cast<const uint4*>(&sm.VN[r][p]);
       }
     }
-    // o = scale * qg S + Aqk v_new
+    // o = qg S + Aqk v_new   (qg carries the output scale)
     if (!kTrans) {
       float acc[1][4][4];
       zero_acc(acc);
       warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.QG[0][0], ScanStage<K>::LK}, m0,
                                          Smem{&sm.Sb[0][0], kScanBV + 8}, n0, 0, K, lane);
-      acc_foreach(acc, m0, n0, lane, [&](float& v, int, int) { v *= a.scale; });
       warp_mma_ks<2, 1, 4, false, false>(acc, Smem{&st.Aqk[0][0], ScanStage<K>::LA}, m0,
                                          Smem{&sm.VN[0][0], kScanBV + 8}, n0, 0, kChunk, lane);
       acc_foreach(acc, m0, n0, lane, [&](float v, int r, int c) { sm.O[r][c] = __float2bfloat16_rn(v); });

@@ -17,13 +17,13 @@ struct ChunkWs {
   __nv_bfloat16* Y;    // A (b k 2^G)           [tokens, H, K]
   __nv_bfloat16* U;    // A (w v)               [tokens, H, V]
   __nv_bfloat16* kg;   // k 2^(G_last - G)      [tokens, H, K]
-  __nv_bfloat16* qg;   // q 2^G                 [tokens, H, K]
+  __nv_bfloat16* qg;   // scale q 2^G           [tokens, H, K]
   __nv_bfloat16* v_new;// [tokens, H, V]
   __nv_bfloat16* h;    // per-chunk entering state, transposed: [NT, H, V, K]
 };
 
 struct BwdWs {
-  __nv_bfloat16* dh;   // state cotangent at the end of each chunk [NT, H, K, V]
+  __nv_bfloat16* dh;   // state cotangent at the end of each chunk, transposed [NT, H, V, K]
   __nv_bfloat16* dvn;  // cotangent of v_new [tokens, H, V]
 };
 
@@ -95,6 +95,8 @@ int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s);
 // tcgen05 forward scan (scan_tc.cu), d_k = d_v = 128
 bool scan_fwd_tc_supported(const gdn2_chunk_args& a);
 int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
+int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                       cudaStream_t s);
 int tc_fault_read(int clear, unsigned int* out);
 
 }  // namespace gdn2

@@ -3,7 +3,7 @@
 #include <cuda_runtime.h>
 
 namespace gdn2 {
-enum KernelId { kKIntra = 0, kKScanFwd, kKScanBwd, kKBwdIntra, kKRecurrent, kKCp, kKScanFwdTc, kNumKernels };
+enum KernelId { kKIntra = 0, kKScanFwd, kKScanBwd, kKBwdIntra, kKRecurrent, kKCp, kKScanFwdTc, kKScanBwdTc, kNumKernels };
 bool prof_on();
 void prof_begin(int id, cudaStream_t s);
 void prof_end(int id, cudaStream_t s);

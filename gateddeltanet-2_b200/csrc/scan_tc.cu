@@ -5,7 +5,8 @@
 // product has M = 128 (the state's V rows):
 //
 //     v_new^T = U^T - S^T Y^T                  (MMA1: S^T Y^T,   N = 64, K = 128)
-//     o^T     = scale S^T qg^T + v_new^T Aqk^T (MMA2 / MMA3,     N = 64, K = 128 / 64)
+//     o^T     = S^T qg^T + v_new^T Aqk^T       (MMA2 / MMA3,     N = 64, K = 128 / 64;
+//                                               qg carries the output scale)
 //     S^T    <- S^T Diag(2^G_last) + v_new^T kg(MMA4,            N = 128, K = 64)
 //
 // One CTA per (sequence, head).  S^T lives in TMEM for the whole sequence
@@ -248,7 +249,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       tc::tc_fence_before();
       tc::mbar_arrive(&sm.vn_ready);
 
-      // step 3: o = scale qg S + Aqk v_new, into the [t][v] tile
+      // step 3: o = qg S + Aqk v_new, into the [t][v] tile
       if (!(ok = warp_wait(&sm.mma34, c & 1))) break;
       tc::tc_fence_after();
       {
@@ -261,7 +262,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           *reinterpret_cast<__nv_bfloat16*>(ot + tc::sw128_off(tb0 + i, v & 63)) =
-              __float2bfloat16_rn(fmaf(a.scale, x1[i], x2[i]));
+              __float2bfloat16_rn(x1[i] + x2[i]);
       }
       tc::fence_proxy_async();
       tc::mbar_arrive(&sm.o_full);
@@ -410,6 +411,312 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
   }
 }
 
+// ===========================================================================
+// Backward state scan (reverse over chunks), transposed like the forward:
+//     dh^T[c]  = dS^T                                  (stored, bf16)
+//     dv^T     = do^T Aqk + dS^T kg^T                   (MMA-a: N = 64, K = 64;
+//                                                        MMA-b: N = 64, K = 128)
+//     dS^T    <- dS^T Diag(2^G_last) + do^T qg - dv^T Y (MMA-c, MMA-d: N = 128, K = 64)
+// (reference: chunk_kda.py:1356-1669 with the dAv of :3769-3831).  do and Aqk
+// enter as N-/M-major operands straight from their TMA tiles; dv^T is written
+// negated as the A operand of MMA-d.  Rows of do past a ragged sequence end
+// are zeroed in shared memory: TMA loads the next sequence's rows there, and
+// MMA-a and MMA-c contract over tokens with no other operand zero there.
+// ===========================================================================
+constexpr uint32_t kColDV = 128;  // dv^T [128 x 64]; dS^T at kColS
+
+struct alignas(1024) BtStage {
+  __nv_bfloat16 DO[2][64 * 64];  // [t][v], two 64-column blocks (M-major A of MMA-a / MMA-c)
+  __nv_bfloat16 KG[2][64 * 64];  // [t][k]   (K-major B of MMA-b)
+  __nv_bfloat16 QG[2][64 * 64];  // [t][k]   (N-major B of MMA-c)
+  __nv_bfloat16 Y[2][64 * 64];   // [t][k]   (N-major B of MMA-d)
+  __nv_bfloat16 Aqk[64 * 64];    // [s][t]   (N-major B of MMA-a)
+  float glast[kTcK];
+};
+
+struct alignas(1024) BtSmem {
+  BtStage st[2];
+  __nv_bfloat16 DSA[2][128 * 64];  // dS^T in bf16, [v][k] (A of MMA-b; also the stored dh^T)
+  __nv_bfloat16 DVA[128 * 64];     // -dv^T in bf16, [v][t] (A of MMA-d)
+  __nv_bfloat16 DVT[2][64 * 64];   // dv in bf16, [t][v] (stored)
+  float D[kTcK];
+  uint64_t full[2], empty[2];
+  uint64_t d_ready, dsa_ready, dsa_free, dv_ready, dva_ready, dvt_free, ds_ready;
+  uint32_t tbase;
+};
+static_assert(sizeof(BtSmem) + 1024 <= 227 * 1024, "tcgen05 backward scan shared memory");
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, const ChunkWs ws, const BwdWs bw,
+                         const __grid_constant__ CUtensorMap tmDO, const __grid_constant__ CUtensorMap tmKG,
+                         const __grid_constant__ CUtensorMap tmQG, const __grid_constant__ CUtensorMap tmY,
+                         const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmDV,
+                         const __grid_constant__ CUtensorMap tmDH) {
+  extern __shared__ unsigned char smem_raw[];
+  BtSmem& sm = *reinterpret_cast<BtSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t H = a.H;
+  const int64_t n = blockIdx.x / H, h = blockIdx.x % H;
+  SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
+  int64_t bos, len;
+  geo.seq(n, bos, len);
+  const int nchunks = (int)((len + kChunk - 1) / kChunk);
+  const int64_t c0 = geo.chunk0(n);
+  // iteration it handles chunk nchunks - 1 - it
+  auto chunk_of = [&](int it) { return nchunks - 1 - it; };
+  auto chunk_len = [&](int c) {
+    const int64_t r = len - (int64_t)c * kChunk;
+    return (int)(r < kChunk ? r : kChunk);
+  };
+
+  if (tid == 0) {
+    tc::mbar_init(&sm.full[0], 1);
+    tc::mbar_init(&sm.full[1], 1);
+    tc::mbar_init(&sm.empty[0], 1);
+    tc::mbar_init(&sm.empty[1], 1);
+    tc::mbar_init(&sm.d_ready, kStateThreads);
+    tc::mbar_init(&sm.dsa_ready, kStateThreads);
+    tc::mbar_init(&sm.dsa_free, 1);
+    tc::mbar_init(&sm.dv_ready, 1);
+    tc::mbar_init(&sm.dva_ready, kStateThreads);
+    tc::mbar_init(&sm.dvt_free, 1);
+    tc::mbar_init(&sm.ds_ready, 1);
+    tc::mbar_fence_init();
+  }
+  if (warp == kWarpMma) tc::tmem_alloc(&sm.tbase, 256);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tb = sm.tbase;
+  bool ok = true;
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ state warps
+    const int qtr = warp & 3, half = warp >> 2;
+    const int v = 32 * qtr + lane;
+    const uint32_t tl = tb + ((uint32_t)(32 * qtr) << 16);
+    const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
+    const int kb0 = 64 * half, tb0 = 32 * half;
+    {
+      const float* d0 = gr.dht ? gr.dht + (n * H + h) * (int64_t)kTcK * kTcV : nullptr;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int k = kb0 + 32 * j + i;
+          x[i] = d0 ? (tr ? d0[(int64_t)v * kTcK + k] : d0[(int64_t)k * kTcV + v]) : 0.f;
+        }
+        tc::tmem_st32(tl + kColS + kb0 + 32 * j, x);
+      }
+      tc::tmem_wait_st();
+    }
+    for (int it = 0; it < nchunks; ++it) {
+      const int s = it & 1, c = chunk_of(it), L = chunk_len(c);
+      BtStage& st = sm.st[s];
+      if (!(ok = warp_wait(&sm.full[s], (it >> 1) & 1))) break;
+      if (half == 0) sm.D[v] = exp2_approx(st.glast[v]);
+      if (L < kChunk) {  // do rows past the sequence end -> 0
+        for (int i = tid; i < (kChunk - L) * 16; i += kStateThreads) {
+          const int t = L + i / 16, piece = i % 16;
+          *reinterpret_cast<uint4*>(reinterpret_cast<char*>(st.DO[piece >> 3]) + t * 128 + ((piece & 7) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      tc::mbar_arrive(&sm.d_ready);
+      if (!(ok = warp_wait(&sm.d_ready, it & 1))) break;
+
+      // step 1: dS^T -> bf16 operand rows (also the stored dh^T); decay in TMEM
+      if (it > 0 && !(ok = warp_wait(&sm.dsa_free, (it - 1) & 1))) break;
+      {
+        char* row = reinterpret_cast<char*>(sm.DSA[half]) + v * 128;
+        float x0[32], x1[32];
+        tc::tmem_ld32(tl + kColS + kb0, x0);
+        tc::tmem_ld32(tl + kColS + kb0 + 32, x1);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          *reinterpret_cast<uint4*>(row + ((q ^ (v & 7)) << 4)) = pack8(x0 + 8 * q);
+          *reinterpret_cast<uint4*>(row + (((4 + q) ^ (v & 7)) << 4)) = pack8(x1 + 8 * q);
+        }
+        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 d = d4[q], e = d4[8 + q];
+          x0[4 * q + 0] *= d.x;
+          x0[4 * q + 1] *= d.y;
+          x0[4 * q + 2] *= d.z;
+          x0[4 * q + 3] *= d.w;
+          x1[4 * q + 0] *= e.x;
+          x1[4 * q + 1] *= e.y;
+          x1[4 * q + 2] *= e.z;
+          x1[4 * q + 3] *= e.w;
+        }
+        tc::tmem_st32(tl + kColS + kb0, x0);
+        tc::tmem_st32(tl + kColS + kb0 + 32, x1);
+      }
+      tc::tmem_wait_st();
+      tc::fence_proxy_async();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.dsa_ready);
+
+      // step 2: dv -> stored tile [t][v] and the negated operand [v][t]
+      if (!(ok = warp_wait(&sm.dv_ready, it & 1))) break;
+      tc::tc_fence_after();
+      {
+        float x[32];
+        tc::tmem_ld32(tl + kColDV + tb0, x);
+        tc::tmem_wait_ld();
+        if (it > 0 && !(ok = warp_wait(&sm.dvt_free, (it - 1) & 1))) break;
+        char* dvt = reinterpret_cast<char*>(sm.DVT[v >> 6]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = tb0 + i;
+          const __nv_bfloat16 dvb = __float2bfloat16_rn(t < L ? x[i] : 0.f);
+          *reinterpret_cast<__nv_bfloat16*>(dvt + tc::sw128_off(t, v & 63)) = dvb;
+          x[i] = -__bfloat162float(dvb);
+        }
+        char* row = reinterpret_cast<char*>(sm.DVA) + v * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+      }
+      tc::fence_proxy_async();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&sm.dva_ready);
+      if (!(ok = warp_wait(&sm.ds_ready, it & 1))) break;
+      tc::tc_fence_after();
+    }
+    if (ok && gr.dh0) {
+      float* d = gr.dh0 + (n * H + h) * (int64_t)kTcK * kTcV;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x[32];
+        tc::tmem_ld32(tl + kColS + kb0 + 32 * j, x);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int k = kb0 + 32 * j + i;
+          if (tr) d[(int64_t)v * kTcK + k] = x[i];
+          else d[(int64_t)k * kTcV + v] = x[i];
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nchunks > 0) {
+      constexpr uint32_t kIdA = tc::idesc_bf16(128, 64, 1, 1);   // M-major do, N-major Aqk
+      constexpr uint32_t kIdB = tc::idesc_bf16(128, 64, 0, 0);   // dS^T, kg
+      constexpr uint32_t kIdC = tc::idesc_bf16(128, 128, 1, 1);  // M-major do, N-major qg
+      constexpr uint32_t kIdD = tc::idesc_bf16(128, 128, 0, 1);  // -dv^T, N-major Y
+      uint64_t* last = nullptr;
+      uint32_t last_par = 0;
+      for (int it = 0; it < nchunks; ++it) {
+        const int s = it & 1;
+        BtStage& st = sm.st[s];
+        if (!(ok = tc::mbar_wait(&sm.full[s], (it >> 1) & 1) && tc::mbar_wait(&sm.dsa_ready, it & 1))) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + kColDV, tc::sdesc_sw128(tc::smem_u32(st.DO[0]) + kk * 2048, kTileBytes, 1024),
+                       tc::sdesc_sw128(tc::smem_u32(st.Aqk) + kk * 2048, kTileBytes, 1024), kIdA, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::mma_bf16(tb + kColDV, kdesc(sm.DSA[kk >> 2], (kk & 3) * 32), kdesc(st.KG[kk >> 2], (kk & 3) * 32),
+                       kIdB, 1);
+        tc::mma_commit(&sm.dv_ready);
+        last = &sm.dv_ready;
+        last_par = it & 1;
+        if (!(ok = tc::mbar_wait(&sm.dva_ready, it & 1))) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + kColS, tc::sdesc_sw128(tc::smem_u32(st.DO[0]) + kk * 2048, kTileBytes, 1024),
+                       tc::sdesc_sw128(tc::smem_u32(st.QG[0]) + kk * 2048, kTileBytes, 1024), kIdC, 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + kColS, kdesc(sm.DVA, kk * 32),
+                       tc::sdesc_sw128(tc::smem_u32(st.Y[0]) + kk * 2048, kTileBytes, 1024), kIdD, 1);
+        tc::mma_commit(&sm.ds_ready);
+        tc::mma_commit(&sm.empty[s]);
+        last = &sm.ds_ready;
+        last_par = it & 1;
+      }
+      if (last && !tc::mbar_wait(last, last_par)) ok = false;
+    }
+  } else if (warp == kWarpLoad) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tc::prefetch_tensormap(&tmDO);
+      tc::prefetch_tensormap(&tmKG);
+      tc::prefetch_tensormap(&tmQG);
+      tc::prefetch_tensormap(&tmY);
+      tc::prefetch_tensormap(&tmA);
+      int it = 0;
+      for (; it < nchunks; ++it) {
+        const int s = it & 1, c = chunk_of(it), L = chunk_len(c);
+        BtStage& st = sm.st[s];
+        if (it >= 2 && !(ok = tc::mbar_wait(&sm.empty[s], ((it >> 1) - 1) & 1))) break;
+        const int64_t t0 = bos + (int64_t)c * kChunk;
+        const int tt = (int)t0, hh = (int)h;
+        tc::mbar_arrive_expect_tx(&sm.full[s], kStageTx);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          tc::tma_load_3d(st.DO[b], &tmDO, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.KG[b], &tmKG, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.QG[b], &tmQG, &sm.full[s], 64 * b, hh, tt);
+          tc::tma_load_3d(st.Y[b], &tmY, &sm.full[s], 64 * b, hh, tt);
+        }
+        tc::tma_load_3d(st.Aqk, &tmA, &sm.full[s], 0, hh, tt);
+        tc::bulk_load(st.glast, ws.G + ((t0 + L - 1) * H + h) * kTcK, kTcK * 4, &sm.full[s]);
+      }
+      for (int j = (it < 2 ? 0 : it - 2); j < it; ++j)
+        if (!tc::mbar_wait(&sm.full[j & 1], (j >> 1) & 1)) ok = false;
+    }
+  } else {
+    // ------------------------------------------------------------ output writer
+    // dh^T from the dS^T operand tile, dv from its [t][v] tile.  The state
+    // warps cannot run more than one phase of dsa_ready / dva_ready ahead of
+    // this warp (they wait for dsa_free / dvt_free before refilling the tiles).
+    for (int it = 0; it < nchunks; ++it) {
+      const int c = chunk_of(it), L = chunk_len(c);
+      const int64_t t0 = bos + (int64_t)c * kChunk;
+      if (!(ok = warp_wait(&sm.dsa_ready, it & 1))) break;
+      if (lane == 0) {
+        const int row = (int)(((c0 + c) * H + h) * kTcV);
+        tc::tma_store_2d(&tmDH, sm.DSA[0], 0, row);
+        tc::tma_store_2d(&tmDH, sm.DSA[1], 64, row);
+        tc::bulk_commit();
+        tc::bulk_wait_read_all();
+        tc::mbar_arrive(&sm.dsa_free);
+      }
+      __syncwarp();
+      if (!(ok = warp_wait(&sm.dva_ready, it & 1))) break;
+      if (L == kChunk) {
+        if (lane == 0) {
+          tc::tma_store_3d(&tmDV, sm.DVT[0], 0, (int)h, (int)t0);
+          tc::tma_store_3d(&tmDV, sm.DVT[1], 64, (int)h, (int)t0);
+          tc::bulk_commit();
+          tc::bulk_wait_read_all();
+        }
+      } else {
+        copy_rows_out(sm.DVT, bw.dvn, t0, H, h, L, lane);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&sm.dvt_free);
+    }
+    if (lane == 0) tc::bulk_wait_all();
+  }
+
+  if (!ok) fault();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tb, 256);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -455,6 +762,11 @@ bool scan_fwd_tc_supported(const gdn2_chunk_args& a) { return a.K == kTcK && a.V
 int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
   const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T, H = (uint64_t)a.H;
   const bool save = a.flags & GDN2_SAVE_FOR_BWD;
+  auto kern = save ? chunk_scan_fwd_tc_kernel<true> : chunk_scan_fwd_tc_kernel<false>;
+  const int smem = (int)sizeof(TcSmem) + 1024;
+  // a runtime call first: it binds this thread's context, which the driver's
+  // tensor-map encoder needs (autograd runs the backward on its own threads)
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   CUtensorMap mY, mQG, mKG, mU, mA, mO, mVN, mH;
   if (!token_map(&mY, ws.Y, kTcK, H, tokens) || !token_map(&mQG, ws.qg, kTcK, H, tokens) ||
       !token_map(&mKG, ws.kg, kTcK, H, tokens) || !token_map(&mU, ws.U, kTcV, H, tokens) ||
@@ -465,11 +777,27 @@ int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t
            : false)
     return GDN2_ERR_TENSOR_MAP;
   if (!save) mVN = mH = mO;  // unused without SAVE_FOR_BWD
-  auto kern = save ? chunk_scan_fwd_tc_kernel<true> : chunk_scan_fwd_tc_kernel<false>;
-  const int smem = (int)sizeof(TcSmem) + 1024;
-  GDN2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   ProfScope ps(kKScanFwdTc, s);
   kern<<<(unsigned)(a.N * a.H), kTcThreads, smem, s>>>(a, ws, mY, mQG, mKG, mU, mA, mO, mVN, mH);
+  GDN2_LAUNCH_CHECK();
+  return 0;
+}
+
+int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                       cudaStream_t s) {
+  const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T, H = (uint64_t)a.H;
+  const int smem = (int)sizeof(BtSmem) + 1024;
+  // binds this thread's context before the driver's tensor-map encoder runs
+  GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  CUtensorMap mDO, mKG, mQG, mY, mA, mDV, mDH;
+  if (!token_map(&mDO, g.dout, kTcV, H, tokens) || !token_map(&mKG, ws.kg, kTcK, H, tokens) ||
+      !token_map(&mQG, ws.qg, kTcK, H, tokens) || !token_map(&mY, ws.Y, kTcK, H, tokens) ||
+      !token_map(&mA, ws.Aqk, kChunk, H, tokens) || !token_map(&mDV, bw.dvn, kTcV, H, tokens) ||
+      !rows_map(&mDH, bw.dh, kTcK, (uint64_t)a.NT * H * kTcV))
+    return GDN2_ERR_TENSOR_MAP;
+  ProfScope ps(kKScanBwdTc, s);
+  chunk_scan_bwd_tc_kernel<<<(unsigned)(a.N * a.H), kTcThreads, smem, s>>>(a, g, ws, bw, mDO, mKG, mQG, mY, mA,
+                                                                             mDV, mDH);
   GDN2_LAUNCH_CHECK();
   return 0;
 }
