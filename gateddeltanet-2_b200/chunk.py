@@ -178,13 +178,13 @@ def _intermediate_states(ws, args, B, T, H, K, V, NT, transpose):
     lib = _lib.load()
     # the h buffer sits right after v_new in the workspace layout; recover it
     # through a second layout query with SAVE (offsets are deterministic)
+    # the workspace keeps each chunk state transposed, [NT, H, V, K]
     off = _ws_offset_of_h(args)
-    h = ws[off:off + NT * H * K * V * 2].view(torch.bfloat16).view(NT, H, K, V)
+    hT = ws[off:off + NT * H * K * V * 2].view(torch.bfloat16).view(NT, H, V, K)
+    h = (hT if transpose else hT.transpose(-1, -2)).contiguous()
     if args.cu_seqlens is None:
-        h = h.view(B, NT // max(B, 1), H, K, V)
-    else:
-        h = h.unsqueeze(0)
-    return h.transpose(-1, -2).contiguous() if transpose else h.clone()
+        return h.view(B, NT // max(B, 1), H, *h.shape[-2:])
+    return h.unsqueeze(0)
 
 
 def _ws_offset_of_h(args) -> int:

@@ -207,6 +207,33 @@ def test_chunk_backward_varlen_matches_oracle(gdn2):
     assert_close(h0_d.grad, r.grads["h0"], "dh0")
 
 
+@pytest.mark.parametrize("K,V,transpose", [(128, 128, False), (128, 128, True), (64, 64, False)])
+def test_intermediate_states_match_oracle_prefix_states(gdn2, K, V, transpose):
+    """return_intermediate_states: h[c] is the state entering chunk c, i.e. the
+    state after the first 64 c tokens (stored in bf16, like the reference's h:
+    the bound adds bf16's relative step, 2^-8)."""
+    B, T, H = 1, 200, 2
+    q, k, v, gg, b, w = _inputs(11, B, T, H, K, V)
+    h0 = torch.randn(B, H, K, V) * 0.1
+    with torch.inference_mode():
+        _, _, hs = gdn2.chunk_gdn2(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), b.cuda(), w.cuda(),
+                                   initial_state=(h0.transpose(-1, -2) if transpose else h0).contiguous().cuda(),
+                                   output_final_state=True, return_intermediate_states=True,
+                                   transpose_state_layout=transpose)
+    torch.cuda.synchronize()
+    assert hs.shape == (B, (T + 63) // 64, H) + ((V, K) if transpose else (K, V))
+    x = [t.float().numpy() for t in (q, k, v, gg, b, w)]
+    for c in range(hs.shape[1]):
+        if c == 0:
+            ref = h0.numpy()
+        else:
+            _, ref, _ = orc.recurrent_fwd(*(t[:, :64 * c] for t in x), K ** -0.5, h0.numpy())
+        got = hs[:, c].float().cpu().numpy()
+        if transpose:
+            got = got.swapaxes(-1, -2)
+        np.testing.assert_allclose(got, ref, rtol=2e-3 + 2 ** -8, atol=1e-2, err_msg=f"h[{c}]")
+
+
 def test_no_bounded_wait_gave_up(gdn2):
     """The tensor-core kernels run above bound every barrier wait; none of
     them may have given up (that would mean invalid results above)."""
