@@ -332,6 +332,8 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       cp_async16b(&p1.VN[r][p], ws.v_new + gi, ok);
       cp_async16b(&p1.DVN[r][p], bw.dvn + gi, ok);
     }
+    cp_commit();  // group 1: the phase-1 operands
+    // group 2: A and G, first needed after the phase-1 products
     for (int i = tid; i < kChunk * (kChunk / 8); i += kBIntraThreads) {
       const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
       const bool ok = r < L;
@@ -345,16 +347,14 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     cp_commit();
     for (int c = tid; c < K; c += kBIntraThreads) sm.last[c] = 0.f;
     if (tid == 0) sm.nflag = 0;
-    cp_wait<0>();
+    cp_wait<1>();
     __syncthreads();
-  }
-  // the forward's exactness flags (same criterion, same G)
-  for (int i = tid; i < 4 * K; i += kBIntraThreads) {
-    const int blk = i / K, c = i % K, a0 = blk * 16;
-    const int alast = min(a0 + 15, max(L - 1, 0));
-    const uint8_t f = (sm.G[a0][c] - sm.G[alast][c]) > kAnchorRangeB ? 1 : 0;
-    sm.flag[blk][c] = f;
-    if (f) atomicAdd(&sm.nflag, 1);
+    // w and v are read from global in the d(w v) step: pull them into L2 now
+    if (tid < 2 * L) {
+      const int r = tid >> 1;
+      if (tid & 1) l2_prefetch(vin + tokV(r, 0), V * 2);
+      else l2_prefetch(static_cast<const TB*>(a.w) + tokV(r, 0), V * (int)sizeof(TB));
+    }
   }
 
   const int rb = warp & 3, ch = warp >> 2;
@@ -378,6 +378,16 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     zero_acc(t);
     warp_mma<1, NTk, false, false>(t, Smem{&p1.DVN[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
     acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { p1.DY[r][c] = __float2bfloat16_rn(-v); });
+  }
+  cp_wait<0>();  // A and G
+  __syncthreads();
+  // the forward's exactness flags (same criterion, same G)
+  for (int i = tid; i < 4 * K; i += kBIntraThreads) {
+    const int blk = i / K, c = i % K, a0 = blk * 16;
+    const int alast = min(a0 + 15, max(L - 1, 0));
+    const uint8_t f = (sm.G[a0][c] - sm.G[alast][c]) > kAnchorRangeB ? 1 : 0;
+    sm.flag[blk][c] = f;
+    if (f) atomicAdd(&sm.nflag, 1);
   }
   // dgk_last = 2^G_last * sum_v h dh  (4 threads per state row)
   {

@@ -129,27 +129,15 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     const bool ok = r < L;
     cp_async16(&sm.G[r][p], a.g + ((t0 + (ok ? r : 0)) * H + h) * K + p, ok);
   }
-  // w (TB) and v (bf16) ride along, parked in the score buffers (free until step 4)
-  {
-    TB* wst = reinterpret_cast<TB*>(&sm.Aqk[0][0]);            // [64][V] TB, fits Aqk+Tm
-    __nv_bfloat16* vst = reinterpret_cast<__nv_bfloat16*>(&sm.Af[0][0]);  // [64][V] bf16
-    constexpr int kWPer16 = 16 / sizeof(TB);
-    for (int i = tid; i < kChunk * (V / kWPer16); i += kIntraThreads) {
-      const int r = i / (V / kWPer16), p = (i % (V / kWPer16)) * kWPer16;
-      const bool ok = r < L;
-      cp_async16(wst + r * V + p, static_cast<const TB*>(a.w) + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
-    }
-    for (int i = tid; i < kChunk * (V / 8); i += kIntraThreads) {
-      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      const bool ok = r < L;
-      cp_async16(vst + r * V + p, vin + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
-    }
-  }
   cp_async_commit();
-  // each thread's b values for steps 3 and 7, issued now: vectors g = tid + 256 u
-  // of 8 consecutive channels (row g / (K/8), channels from 8 (g % (K/8)))
+  cp_async_wait<0>();
+  __syncthreads();
+  // Only q, k and g gate the first steps.  b (registers, needed from step 3)
+  // is requested now and w, v (needed by the last product) once the score
+  // operands are dead (after step 4), so their HBM traffic overlaps compute
+  // instead of lengthening the first wait.
   constexpr int kVec = kChunk * K / 8 / kIntraThreads;
-  float breg[kVec][8];
+  float breg[kVec][8];  // vectors g = tid + 256 u: row g / (K/8), channels from 8 (g % (K/8))
 #pragma unroll
   for (int u = 0; u < kVec; ++u) {
     const int g = tid + u * kIntraThreads, r = g / (K / 8), c0 = (g % (K / 8)) * 8;
@@ -158,21 +146,6 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) breg[u][e] = 0.f;
-    }
-  }
-  cp_async_wait<0>();
-  __syncthreads();
-  {
-    const TB* wst = reinterpret_cast<const TB*>(&sm.Aqk[0][0]);
-    const __nv_bfloat16* vst = reinterpret_cast<const __nv_bfloat16*>(&sm.Af[0][0]);
-    for (int g = tid; g < kChunk * V / 8; g += kIntraThreads) {
-      const int r = g / (V / 8), c0 = (g % (V / 8)) * 8;
-      float w8[8], v8[8];
-      ld8(wst + r * V + c0, w8);
-      ld8(vst + r * V + c0, v8);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) w8[e] *= v8[e];
-      st8(&sm.WV[r][c0], w8);
     }
   }
   if (l2) {
@@ -340,6 +313,27 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   }
   __syncthreads();
 
+  // w (TB) and v (bf16) into the score-operand region, dead until step 7's
+  // operands are built (they land while steps 5-6 run).  Where they do not
+  // fit (d_k = 64 with fp32 w), step 7 reads them from global instead.
+  constexpr bool kStageWV = kChunk * V * (sizeof(TB) + 2) <= sizeof(sm.u);
+  TB* wst = reinterpret_cast<TB*>(&sm.u.s.QG[0][0]);  // [64][V] TB
+  __nv_bfloat16* vst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(wst) + kChunk * V * sizeof(TB));
+  if constexpr (kStageWV) {
+    constexpr int kWPer16 = 16 / sizeof(TB);
+    for (int i = tid; i < kChunk * (V / kWPer16); i += kIntraThreads) {
+      const int r = i / (V / kWPer16), p = (i % (V / kWPer16)) * kWPer16;
+      const bool ok = r < L;
+      cp_async16(wst + r * V + p, static_cast<const TB*>(a.w) + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
+    }
+    for (int i = tid; i < kChunk * (V / 8); i += kIntraThreads) {
+      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+      const bool ok = r < L;
+      cp_async16(vst + r * V + p, vin + ((t0 + (ok ? r : 0)) * H + h) * V + p, ok);
+    }
+    cp_async_commit();
+  }
+
   // ---- 5. exact pairs for (block, channel)s beyond the anchored range ------
   for (int blk = 0; blk < 4; ++blk) {
     if (sm.nflag[blk] == 0) continue;
@@ -444,7 +438,28 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       st8(ws.Aqk + gi, aq);
     }
   }
-  // WY operands (the score operands are dead now)
+  // w v for the U product; rows past the sequence end are zero
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int g = tid; g < kChunk * V / 8; g += kIntraThreads) {
+    const int r = g / (V / 8), c0 = (g % (V / 8)) * 8;
+    float w8[8], v8[8];
+    if constexpr (kStageWV) {
+      ld8(wst + r * V + c0, w8);
+      ld8(vst + r * V + c0, v8);
+    } else if (r < L) {
+      const int64_t gi = ((t0 + r) * H + h) * V + c0;
+      ld8(static_cast<const TB*>(a.w) + gi, w8);
+      ld8(vin + gi, v8);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w8[e] = v8[e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w8[e] *= v8[e];
+    st8(&sm.WV[r][c0], w8);
+  }
+  // WY operands (the score operands and the staged w, v are dead now)
   __syncthreads();
   {
 #pragma unroll

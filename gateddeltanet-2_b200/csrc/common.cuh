@@ -54,6 +54,11 @@ GDN2_DEV void ld8(const __nv_bfloat16* p, float* x) {
     x[2 * i + 1] = __high2float(h2);
   }
 }
+// pulls [p, p + bytes) into L2 without waiting (p 16-byte aligned, bytes % 16 == 0)
+GDN2_DEV void l2_prefetch(const void* p, int bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // 2 consecutive elements (8-byte aligned for fp32, 4-byte for bf16)
 GDN2_DEV float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 GDN2_DEV float2 ld2(const __nv_bfloat16* p) {
