@@ -214,6 +214,7 @@ struct BIntraSmem {
   // padded rows: accumulator-pattern accesses (8 rows x 4 column pairs per
   // warp instruction) then fall in distinct banks
   static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 8, LG = K + 4;
+  static constexpr int LB = K + 16 / (int)sizeof(TB);  // staged db rows (16-byte aligned)
   alignas(16) float G[kChunk][LG];         // later reused for dG
   alignas(16) __nv_bfloat16 A[kChunk][LA];
   alignas(16) __nv_bfloat16 DAqk[kChunk][LA];
@@ -389,17 +390,21 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     sm.flag[blk][c] = f;
     if (f) atomicAdd(&sm.nflag, 1);
   }
-  // dgk_last = 2^G_last * sum_v h dh  (4 threads per state row)
+  // dgk_last = 2^G_last * sum_v h dh: a thread owns two state rows and a
+  // slice of v (paired loads along the rows, conflict-free), partials summed
+  // into last[] with shared atomics
   {
-    const int r = tid >> 2, part = tid & 3;
-    float s = 0.f;
-    if (r < K) {
-      for (int v = part * (V / 4); v < (part + 1) * (V / 4); ++v)
-        s += __bfloat162float(p1.HsT[v][r]) * __bfloat162float(p1.DHT[v][r]);
+    constexpr int kPairs = K / 2, kParts = kBIntraThreads / kPairs, kVPer = V / kParts;
+    const int r = 2 * (tid % kPairs), part = tid / kPairs;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll 4
+    for (int v = part * kVPer; v < (part + 1) * kVPer; ++v) {
+      const float2 hh = ld2(&p1.HsT[v][r]), dd = ld2(&p1.DHT[v][r]);
+      s0 += hh.x * dd.x;
+      s1 += hh.y * dd.y;
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    if (r < K && part == 0) atomicAdd(&sm.last[r], s * exp2_approx(Glast[r]));
+    atomicAdd(&sm.last[r], s0 * exp2_approx(Glast[r]));
+    atomicAdd(&sm.last[r + 1], s1 * exp2_approx(Glast[r + 1]));
   }
   // dAqk = scale do v_new^T (lower incl. diagonal)
   {
@@ -737,19 +742,19 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
   __syncthreads();
   {
-    __nv_bfloat16* dqo = static_cast<__nv_bfloat16*>(gr.dq);
-    __nv_bfloat16* dko = static_cast<__nv_bfloat16*>(gr.dk);
-    TB* dbo = static_cast<TB*>(gr.db);
+    // staged in the phase-3 operand region (dead now), written out below
+    __nv_bfloat16 (*sdq)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.QG[0][0]);
+    __nv_bfloat16 (*sdk)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.KBG[0][0]);
+    TB (*sdb)[S::LB] = reinterpret_cast<TB (*)[S::LB]>(&p3.KN[0][0]);
+    static_assert(kChunk * S::LB * sizeof(TB) <= sizeof(p3.KN), "staged db fits the KN operand");
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         const int r = m0 + (lane >> 2) + x * 8, c = n0 + 8 * j + 2 * (lane & 3);
-        if (r >= L) continue;
-        const int64_t gi = tokK(r, c);
         float xq0 = dq[0][j][2 * x], xq1 = dq[0][j][2 * x + 1];
         float xk0 = dk[0][j][2 * x], xk1 = dk[0][j][2 * x + 1];
-        if (l2) {
+        if (l2 && r < L) {
           float sq = 0.f, sk = 0.f;
 #pragma unroll
           for (int y = 0; y < 4; ++y) {
@@ -757,15 +762,31 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
             sk += sm.rsum[r][y][1];
           }
           const float rq = ws.q_rstd[(t0 + r) * H + h], rk = ws.k_rstd[(t0 + r) * H + h];
-          xq0 = (xq0 - sq * qv(r, c)) * rq;
-          xq1 = (xq1 - sq * qv(r, c + 1)) * rq;
-          xk0 = (xk0 - sk * kv(r, c)) * rk;
-          xk1 = (xk1 - sk * kv(r, c + 1)) * rk;
+          const float2 q2 = ld2(&sg.Q[r][c]), k2 = ld2(&sg.Kk[r][c]);
+          xq0 = (xq0 - sq * q2.x) * rq;
+          xq1 = (xq1 - sq * q2.y) * rq;
+          xk0 = (xk0 - sk * k2.x) * rk;
+          xk1 = (xk1 - sk * k2.y) * rk;
         }
-        *reinterpret_cast<__nv_bfloat162*>(dqo + gi) = __floats2bfloat162_rn(xq0, xq1);
-        *reinterpret_cast<__nv_bfloat162*>(dko + gi) = __floats2bfloat162_rn(xk0, xk1);
-        store2<TB>(dbo + gi, db[0][j][2 * x], db[0][j][2 * x + 1]);
+        *reinterpret_cast<__nv_bfloat162*>(&sdq[r][c]) = __floats2bfloat162_rn(xq0, xq1);
+        *reinterpret_cast<__nv_bfloat162*>(&sdk[r][c]) = __floats2bfloat162_rn(xk0, xk1);
+        store2<TB>(&sdb[r][c], db[0][j][2 * x], db[0][j][2 * x + 1]);
       }
+    __syncthreads();
+    __nv_bfloat16* dqo = static_cast<__nv_bfloat16*>(gr.dq);
+    __nv_bfloat16* dko = static_cast<__nv_bfloat16*>(gr.dk);
+    TB* dbo = static_cast<TB*>(gr.db);
+    for (int i = tid; i < L * (K / 8); i += kBIntraThreads) {
+      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+      const int64_t gi = tokK(r, p);
+      *reinterpret_cast<uint4*>(dqo + gi) = *reinterpret_cast<const uint4*>(&sdq[r][p]);
+      *reinterpret_cast<uint4*>(dko + gi) = *reinterpret_cast<const uint4*>(&sdk[r][p]);
+    }
+    constexpr int kBPer16 = 16 / sizeof(TB);
+    for (int i = tid; i < L * (K / kBPer16); i += kBIntraThreads) {
+      const int r = i / (K / kBPer16), p = (i % (K / kBPer16)) * kBPer16;
+      *reinterpret_cast<uint4*>(dbo + tokK(r, p)) = *reinterpret_cast<const uint4*>(&sdb[r][p]);
+    }
   }
   // dg: reverse cumsum inside the chunk, then the gate VJP.  All threads take
   // part: channel c = tid % K, row part p = tid / K (kParts parts of the chunk).
