@@ -431,7 +431,10 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
   cp_commit();
   // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv); the same registers of
-  // w and v also form WV = w v for phase 2 (w, v are read from HBM once)
+  // w and v also form WV = w v for phase 2 (w, v are read from HBM once).  dv
+  // is staged in the WY operand tile (free until phase 2) for 16-byte stores.
+  constexpr bool kStageDv = K == V;
+  __nv_bfloat16 (*sdv)[S::LV] = reinterpret_cast<__nv_bfloat16 (*)[S::LV]>(&p2.KB2G[0][0]);
   {
     __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
     TB* dw = static_cast<TB*>(gr.dw);
@@ -462,16 +465,25 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         const int r = m0 + (lane >> 2) + x * 8, c = n0v + 8 * j + 2 * (lane & 3);
         *reinterpret_cast<__nv_bfloat162*>(&p2.WV[r][c]) =
             __floats2bfloat162_rn(wl[j][2 * x] * vl[j][2 * x], wl[j][2 * x + 1] * vl[j][2 * x + 1]);
+        const __nv_bfloat162 dv2 =
+            __floats2bfloat162_rn(t[0][j][2 * x] * wl[j][2 * x], t[0][j][2 * x + 1] * wl[j][2 * x + 1]);
+        if constexpr (kStageDv) *reinterpret_cast<__nv_bfloat162*>(&sdv[r][c]) = dv2;
         if (r < L) {
           const int64_t gi = tokV(r, c);
-          *reinterpret_cast<__nv_bfloat162*>(dv + gi) =
-              __floats2bfloat162_rn(t[0][j][2 * x] * wl[j][2 * x], t[0][j][2 * x + 1] * wl[j][2 * x + 1]);
+          if constexpr (!kStageDv) *reinterpret_cast<__nv_bfloat162*>(dv + gi) = dv2;
           store2<TB>(dw + gi, t[0][j][2 * x] * vl[j][2 * x], t[0][j][2 * x + 1] * vl[j][2 * x + 1]);
         }
       }
   }
   cp_wait<0>();
   __syncthreads();
+  if constexpr (kStageDv) {  // dv out of its staging tile with 16-byte stores
+    __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
+    for (int i = tid; i < L * (V / 8); i += kBIntraThreads) {
+      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+      *reinterpret_cast<uint4*>(dv + tokV(r, p)) = *reinterpret_cast<const uint4*>(&sdv[r][p]);
+    }
+  }
   // inter-chunk parts: dq = scale (do h^T) 2^G ; dk = (v_new dh^T) 2^(G_last - G)
   {
     float colsum[NTk][2];
@@ -507,6 +519,8 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         if (lane < 4) atomicAdd(&sm.last[n0 + 8 * j + 2 * lane + x], s);
       }
   }
+
+  if constexpr (kStageDv) __syncthreads();  // the staged dv is read before KB2G overwrites it
 
   // ---- phase 2: WY factors -----------------------------------------------------
   for (int g = tid; g < kChunk * K / 8; g += kBIntraThreads) {

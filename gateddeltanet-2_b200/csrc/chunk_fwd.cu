@@ -295,7 +295,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     zero_acc(acc);
     Smem Aop{mat == 0 ? &sm.u.s.QG[0][0] : &sm.u.s.KBG[0][0], S::LK};
     Smem Bop{&sm.u.s.KN[anchor_row0(bi)][0], S::LK};
-    warp_mma<1, 2, false, true>(acc, Aop, bi * 16, Bop, bj * 16, 0, K, lane);
+    warp_mma_ks<4, 1, 2, false, true>(acc, Aop, bi * 16, Bop, bj * 16, 0, K, lane);  // 4 chains of 2 steps
     const float sc = mat == 0 ? a.scale : 1.f;
     acc_foreach(acc, bi * 16, bj * 16, lane, [&](float v, int r, int s) {
       const bool keep = (mat == 0 ? s <= r : s < r) && r < L;
@@ -335,7 +335,8 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
   }
 
   // ---- 5. exact pairs for (block, channel)s beyond the anchored range ------
-  for (int blk = 0; blk < 4; ++blk) {
+  const bool any_flag = (sm.nflag[0] | sm.nflag[1] | sm.nflag[2] | sm.nflag[3]) != 0;  // uniform
+  for (int blk = 0; any_flag && blk < 4; ++blk) {
     if (sm.nflag[blk] == 0) continue;
     if (tid < 136) {
       int rr = 0, p = tid;  // pair index -> (r >= s) inside the 16x16 block
@@ -361,7 +362,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
       }
     }
   }
-  __syncthreads();
+  if (any_flag) __syncthreads();
 
   // ---- 6. A = (I + T)^-1 (fp32) --------------------------------------------
   // 6a: diagonal 16x16 blocks by forward substitution; warp b < 4 owns block b,
