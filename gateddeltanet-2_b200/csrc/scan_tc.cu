@@ -48,11 +48,14 @@ constexpr int kWarpMma = 8, kWarpLoad = 9, kWarpStore = 10;
 constexpr uint32_t kTileBytes = 64 * 64 * 2;  // one [64 x 64] bf16 swizzled tile
 constexpr uint32_t kStageTx = 9 * kTileBytes + kTcK * 4;
 
-// TMEM columns (fp32, 128 lanes)
-constexpr uint32_t kColS = 0;      // S^T            [128 x 128]
-constexpr uint32_t kColAV = 128;   // S^T Y^T        [128 x 64]  } one N = 128 product
-constexpr uint32_t kColAO1 = 192;  // S^T qg^T       [128 x 64]  }
-constexpr uint32_t kColAO2 = 256;  // v_new^T Aqk^T  [128 x 64]
+// TMEM columns (fp32, 128 lanes).  The per-chunk products alternate between
+// two column sets by chunk parity p, so a chunk's output can still be read
+// while the next chunk's products run.
+constexpr uint32_t kColS = 0;  // S^T [128 x 128]
+// S^T Y^T [128 x 64] (one N = 128 product with the next)
+GDN2_DEV constexpr uint32_t col_av(int p) { return 128 + 128 * p; }
+// S^T qg^T + v_new^T Aqk^T = o^T [128 x 64]
+GDN2_DEV constexpr uint32_t col_ao(int p) { return 192 + 128 * p; }
 constexpr uint32_t kTmemCols = 512;
 
 struct alignas(1024) TcStage {
@@ -61,6 +64,7 @@ struct alignas(1024) TcStage {
   __nv_bfloat16 U[2][64 * 64];    // [t][v]; overwritten in place by v_new
   __nv_bfloat16 Aqk[64 * 64];     // [t][s]
   float glast[kTcK];              // G of the chunk's last token (log2 units)
+  float D[kTcK];                  // 2^glast, filled by the producer warp
 };
 
 struct alignas(1024) TcSmem {
@@ -68,9 +72,8 @@ struct alignas(1024) TcSmem {
   __nv_bfloat16 SA[2][128 * 64];  // S^T in bf16, [v][k], two 64-column blocks
   __nv_bfloat16 VN[128 * 64];     // v_new^T in bf16, [v][t]
   __nv_bfloat16 OT[2][64 * 64];   // o in bf16, [t][v], two 64-column blocks
-  float D[kTcK];                  // 2^G_last of the current chunk
-  uint64_t full[2], empty[2];
-  uint64_t d_ready, sa_ready, sa_free, mma12, vn_ready, mma34, o_full, ot_free;
+  uint64_t full[2], empty[2], dready[2];
+  uint64_t sa_ready, sa_free, mma12, vn_ready, mma34, o_full, ot_free;
   uint32_t tbase;
 };
 static_assert(sizeof(TcSmem) + 1024 <= 227 * 1024, "tcgen05 scan shared memory");
@@ -128,7 +131,8 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
     tc::mbar_init(&sm.full[1], 1);
     tc::mbar_init(&sm.empty[0], 2);  // the MMAs' commit + the v_new store having read U
     tc::mbar_init(&sm.empty[1], 2);
-    tc::mbar_init(&sm.d_ready, kStateThreads);
+    tc::mbar_init(&sm.dready[0], 32);  // the producer warp's lanes, D of the stage written
+    tc::mbar_init(&sm.dready[1], 32);
     tc::mbar_init(&sm.sa_ready, kStateThreads);
     tc::mbar_init(&sm.sa_free, 1);
     tc::mbar_init(&sm.mma12, 1);
@@ -167,14 +171,26 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       }
       tc::tmem_wait_st();
     }
+    // o of chunk cc into the [t][v] tile; runs while chunk cc + 1's first
+    // product executes (its accumulator columns alternate by parity)
+    auto output = [&](int cc) -> bool {
+      float x[32];
+      tc::tmem_ld32(tl + col_ao(cc & 1) + tb0, x);
+      tc::tmem_wait_ld();
+      if (cc > 0 && !warp_wait(&sm.ot_free, (cc - 1) & 1)) return false;
+      char* ot = reinterpret_cast<char*>(sm.OT[v >> 6]);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        *reinterpret_cast<__nv_bfloat16*>(ot + tc::sw128_off(tb0 + i, v & 63)) = __float2bfloat16_rn(x[i]);
+      tc::fence_proxy_async();
+      tc::mbar_arrive(&sm.o_full);
+      return true;
+    };
     for (int c = 0; c < nchunks; ++c) {
       const int s = c & 1;
       TcStage& st = sm.st[s];
       const int L = chunk_len(c);
-      if (!(ok = warp_wait(&sm.full[s], (c >> 1) & 1))) break;
-      if (half == 0) sm.D[v] = exp2_approx(st.glast[v]);
-      tc::mbar_arrive(&sm.d_ready);
-      if (!(ok = warp_wait(&sm.d_ready, c & 1))) break;
+      if (!(ok = warp_wait(&sm.dready[s], (c >> 1) & 1))) break;  // the stage and its D
 
       // step 1: entering state -> bf16 operand rows (also the saved h^T); decay in TMEM
       if (kSave && c > 0 && !(ok = warp_wait(&sm.sa_free, (c - 1) & 1))) break;
@@ -189,7 +205,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
           *reinterpret_cast<uint4*>(sarow + ((q ^ (v & 7)) << 4)) = pack8(x0 + 8 * q);
           *reinterpret_cast<uint4*>(sarow + (((4 + q) ^ (v & 7)) << 4)) = pack8(x1 + 8 * q);
         }
-        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0);
+        const float4* d4 = reinterpret_cast<const float4*>(st.D + kb0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 d = d4[q], e = d4[8 + q];
@@ -209,6 +225,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       tc::fence_proxy_async();
       tc::tc_fence_before();
       tc::mbar_arrive(&sm.sa_ready);
+      if (c > 0 && !(ok = output(c - 1))) break;
 
       // step 2: v_new = U - (S^T Y^T)^T, in place over U and as the MMA operand
       if (!(ok = warp_wait(&sm.mma12, c & 1))) break;
@@ -216,7 +233,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       {
         // this thread's U column (32 tokens), read while the TMEM load is in flight
         float x[32];
-        tc::tmem_ld32(tl + kColAV + tb0, x);
+        tc::tmem_ld32(tl + col_av(c & 1) + tb0, x);
         __nv_bfloat16* ucol = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(st.U[v >> 6]) +
                                                             ((v & 7) << 1));
         const int vb = (v & 63) >> 3;
@@ -249,24 +266,11 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
       tc::tc_fence_before();
       tc::mbar_arrive(&sm.vn_ready);
 
-      // step 3: o = qg S + Aqk v_new, into the [t][v] tile
+      // the chunk's products are complete: S is updated, o is in TMEM
       if (!(ok = warp_wait(&sm.mma34, c & 1))) break;
       tc::tc_fence_after();
-      {
-        float x1[32], x2[32];
-        tc::tmem_ld32(tl + kColAO1 + tb0, x1);
-        tc::tmem_ld32(tl + kColAO2 + tb0, x2);
-        tc::tmem_wait_ld();
-        if (c > 0 && !(ok = warp_wait(&sm.ot_free, (c - 1) & 1))) break;
-        char* ot = reinterpret_cast<char*>(sm.OT[v >> 6]);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          *reinterpret_cast<__nv_bfloat16*>(ot + tc::sw128_off(tb0 + i, v & 63)) =
-              __float2bfloat16_rn(x1[i] + x2[i]);
-      }
-      tc::fence_proxy_async();
-      tc::mbar_arrive(&sm.o_full);
     }
+    if (ok && nchunks > 0) ok = output(nchunks - 1);
     if (ok && (a.flags & GDN2_STORE_FINAL)) {
       float* ht = a.ht + (n * H + h) * (int64_t)kTcK * kTcV;
 #pragma unroll
@@ -298,8 +302,8 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
         // [S^T Y^T | S^T qg^T] = S^T [Y; qg]^T
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::mma_bf16(tb + kColAV, kdesc(sm.SA[kk >> 2], (kk & 3) * 32), kdesc(st.YQ[kk >> 2], (kk & 3) * 32),
-                       kId128, kk > 0);
+          tc::mma_bf16(tb + col_av(c & 1), kdesc(sm.SA[kk >> 2], (kk & 3) * 32),
+                       kdesc(st.YQ[kk >> 2], (kk & 3) * 32), kId128, kk > 0);
         tc::mma_commit(&sm.mma12);
         last = &sm.mma12;
         last_par = c & 1;
@@ -307,7 +311,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
         tc::tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc::mma_bf16(tb + kColAO2, kdesc(sm.VN, kk * 32), kdesc(st.Aqk, kk * 32), kId64, kk > 0);
+          tc::mma_bf16(tb + col_ao(c & 1), kdesc(sm.VN, kk * 32), kdesc(st.Aqk, kk * 32), kId64, 1);
         // kg as an N-major operand: 64-column blocks 8 KB apart, 8-row groups 1 KB apart
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -323,17 +327,21 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
     }
   } else if (warp == kWarpLoad) {
     // ------------------------------------------------------------ TMA producer
+    // lane 0 issues the loads; once a stage has landed the whole warp turns its
+    // G_last into the decay D = 2^G_last and publishes it (dready)
     if (lane == 0) {
       tc::prefetch_tensormap(&tmY);
       tc::prefetch_tensormap(&tmQG);
       tc::prefetch_tensormap(&tmKG);
       tc::prefetch_tensormap(&tmU);
       tc::prefetch_tensormap(&tmA);
-      int c = 0;
-      for (; c < nchunks; ++c) {
-        const int s = c & 1;
-        TcStage& st = sm.st[s];
-        if (c >= 2 && !(ok = tc::mbar_wait(&sm.empty[s], ((c >> 1) - 1) & 1))) break;
+    }
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int s = c & 1;
+      TcStage& st = sm.st[s];
+      if (c >= 2 && !(ok = warp_wait(&sm.empty[s], ((c >> 1) - 1) & 1))) break;
+      if (lane == 0) {
         const int64_t t0 = bos + (int64_t)c * kChunk;
         const int L = chunk_len(c);
         const int tt = (int)t0, hh = (int)h;
@@ -348,55 +356,77 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
         tc::tma_load_3d(st.Aqk, &tmA, &sm.full[s], 0, hh, tt);
         tc::bulk_load(st.glast, ws.G + ((t0 + L - 1) * H + h) * kTcK, kTcK * 4, &sm.full[s]);
       }
-      // loads in flight land before the CTA exits
-      for (int j = (c < 2 ? 0 : c - 2); j < c; ++j)
-        if (!tc::mbar_wait(&sm.full[j & 1], (j >> 1) & 1)) ok = false;
+      __syncwarp();
+      if (!(ok = warp_wait(&sm.full[s], (c >> 1) & 1))) break;
+#pragma unroll
+      for (int j = 0; j < kTcK / 32; ++j) st.D[lane + 32 * j] = exp2_approx(st.glast[lane + 32 * j]);
+      tc::mbar_arrive(&sm.dready[s]);
     }
+    // a load in flight (only after a wait gave up) lands before the CTA exits
+    if (!ok && c < nchunks) tc::mbar_wait(&sm.full[c & 1], (c >> 1) & 1);
   } else {
     // ------------------------------------------------------------ output writer
-    // The state warps cannot run more than one phase of sa_ready or o_full
-    // ahead of this warp (they wait for sa_free before the next operand tile
-    // and for ot_free before the next o tile); o_full follows their in-place
-    // v_new writes of the same chunk.
+    // Per chunk c: h^T of c (from the S^T operand tile), o of chunk c - 1 (its
+    // output step runs during chunk c), v_new of c (in place over the U tile),
+    // then the releases.  Every release (sa_free, ot_free, the stage's empty)
+    // follows this warp's wait on vn_ready(c), which keeps the state warps
+    // within one phase of each barrier this warp waits on.
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.o);
+    auto store_o = [&](int cc) {
+      const int64_t t0 = bos + (int64_t)cc * kChunk;
+      const int L = chunk_len(cc);
+      if (L == kChunk) {
+        if (lane == 0) {
+          tc::tma_store_3d(&tmO, sm.OT[0], 0, (int)h, (int)t0);
+          tc::tma_store_3d(&tmO, sm.OT[1], 64, (int)h, (int)t0);
+          tc::bulk_commit();
+        }
+      } else {
+        copy_rows_out(sm.OT, o, t0, H, h, L, lane);
+      }
+    };
     for (int c = 0; c < nchunks; ++c) {
       const int s = c & 1;
       TcStage& st = sm.st[s];
       const int64_t t0 = bos + (int64_t)c * kChunk;
       const int L = chunk_len(c);
       if (kSave) {
-        // h^T of this chunk straight out of the S^T operand tile
         if (!(ok = warp_wait(&sm.sa_ready, c & 1))) break;
         if (lane == 0) {
           const int row = (int)(((c0 + c) * H + h) * kTcV);
           tc::tma_store_2d(&tmH, sm.SA[0], 0, row);
           tc::tma_store_2d(&tmH, sm.SA[1], 64, row);
           tc::bulk_commit();
-          tc::bulk_wait_read_all();
-          tc::mbar_arrive(&sm.sa_free);
         }
-        __syncwarp();
       }
-      if (!(ok = warp_wait(&sm.o_full, c & 1))) break;
-      if (L == kChunk) {
-        if (lane == 0) {
-          if (kSave) {
+      if (c > 0) {
+        if (!(ok = warp_wait(&sm.o_full, (c - 1) & 1))) break;
+        store_o(c - 1);
+      }
+      if (!(ok = warp_wait(&sm.vn_ready, c & 1))) break;
+      if (kSave) {
+        if (L == kChunk) {
+          if (lane == 0) {
             tc::tma_store_3d(&tmVN, st.U[0], 0, (int)h, (int)t0);
             tc::tma_store_3d(&tmVN, st.U[1], 64, (int)h, (int)t0);
+            tc::bulk_commit();
           }
-          tc::tma_store_3d(&tmO, sm.OT[0], 0, (int)h, (int)t0);
-          tc::tma_store_3d(&tmO, sm.OT[1], 64, (int)h, (int)t0);
-          tc::bulk_commit();
-          tc::bulk_wait_read_all();
+        } else {
+          copy_rows_out(st.U, ws.v_new, t0, H, h, L, lane);
         }
-      } else {
-        if (kSave) copy_rows_out(st.U, ws.v_new, t0, H, h, L, lane);
-        copy_rows_out(sm.OT, o, t0, H, h, L, lane);
       }
+      if (lane == 0) tc::bulk_wait_read_all();
       __syncwarp();
       if (lane == 0) {
+        if (kSave) tc::mbar_arrive(&sm.sa_free);
+        if (c > 0) tc::mbar_arrive(&sm.ot_free);
         tc::mbar_arrive(&sm.empty[s]);
-        tc::mbar_arrive(&sm.ot_free);
+      }
+    }
+    if (ok && nchunks > 0) {
+      if ((ok = warp_wait(&sm.o_full, (nchunks - 1) & 1))) {
+        store_o(nchunks - 1);
+        if (lane == 0) tc::bulk_wait_read_all();
       }
     }
     if (lane == 0) tc::bulk_wait_all();
@@ -432,6 +462,7 @@ struct alignas(1024) BtStage {
   __nv_bfloat16 Y[2][64 * 64];   // [t][k]   (N-major B of MMA-d)
   __nv_bfloat16 Aqk[64 * 64];    // [s][t]   (N-major B of MMA-a)
   float glast[kTcK];
+  float D[kTcK];                 // 2^glast, filled by the producer warp
 };
 
 struct alignas(1024) BtSmem {
@@ -439,9 +470,8 @@ struct alignas(1024) BtSmem {
   __nv_bfloat16 DSA[2][128 * 64];  // dS^T in bf16, [v][k] (A of MMA-b; also the stored dh^T)
   __nv_bfloat16 DVA[128 * 64];     // -dv^T in bf16, [v][t] (A of MMA-d)
   __nv_bfloat16 DVT[2][64 * 64];   // dv in bf16, [t][v] (stored)
-  float D[kTcK];
-  uint64_t full[2], empty[2];
-  uint64_t d_ready, dsa_ready, dsa_free, dv_ready, dva_ready, dvt_free, ds_ready;
+  uint64_t full[2], empty[2], dready[2];
+  uint64_t dsa_ready, dsa_free, dv_ready, dva_ready, dvt_free, ds_ready;
   uint32_t tbase;
 };
 static_assert(sizeof(BtSmem) + 1024 <= 227 * 1024, "tcgen05 backward scan shared memory");
@@ -474,7 +504,8 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
     tc::mbar_init(&sm.full[1], 1);
     tc::mbar_init(&sm.empty[0], 1);
     tc::mbar_init(&sm.empty[1], 1);
-    tc::mbar_init(&sm.d_ready, kStateThreads);
+    tc::mbar_init(&sm.dready[0], 32);
+    tc::mbar_init(&sm.dready[1], 32);
     tc::mbar_init(&sm.dsa_ready, kStateThreads);
     tc::mbar_init(&sm.dsa_free, 1);
     tc::mbar_init(&sm.dv_ready, 1);
@@ -514,8 +545,7 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
     for (int it = 0; it < nchunks; ++it) {
       const int s = it & 1, c = chunk_of(it), L = chunk_len(c);
       BtStage& st = sm.st[s];
-      if (!(ok = warp_wait(&sm.full[s], (it >> 1) & 1))) break;
-      if (half == 0) sm.D[v] = exp2_approx(st.glast[v]);
+      if (!(ok = warp_wait(&sm.dready[s], (it >> 1) & 1))) break;  // the stage and its D
       if (L < kChunk) {  // do rows past the sequence end -> 0
         for (int i = tid; i < (kChunk - L) * 16; i += kStateThreads) {
           const int t = L + i / 16, piece = i % 16;
@@ -523,8 +553,6 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
               make_uint4(0u, 0u, 0u, 0u);
         }
       }
-      tc::mbar_arrive(&sm.d_ready);
-      if (!(ok = warp_wait(&sm.d_ready, it & 1))) break;
 
       // step 1: dS^T -> bf16 operand rows (also the stored dh^T); decay in TMEM
       if (it > 0 && !(ok = warp_wait(&sm.dsa_free, (it - 1) & 1))) break;
@@ -539,7 +567,7 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
           *reinterpret_cast<uint4*>(row + ((q ^ (v & 7)) << 4)) = pack8(x0 + 8 * q);
           *reinterpret_cast<uint4*>(row + (((4 + q) ^ (v & 7)) << 4)) = pack8(x1 + 8 * q);
         }
-        const float4* d4 = reinterpret_cast<const float4*>(sm.D + kb0);
+        const float4* d4 = reinterpret_cast<const float4*>(st.D + kb0);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 d = d4[q], e = d4[8 + q];
@@ -646,17 +674,21 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
     }
   } else if (warp == kWarpLoad) {
     // ------------------------------------------------------------ TMA producer
+    // lane 0 issues the loads; once a stage has landed the whole warp writes its
+    // decay D = 2^G_last and publishes it (dready)
     if (lane == 0) {
       tc::prefetch_tensormap(&tmDO);
       tc::prefetch_tensormap(&tmKG);
       tc::prefetch_tensormap(&tmQG);
       tc::prefetch_tensormap(&tmY);
       tc::prefetch_tensormap(&tmA);
-      int it = 0;
-      for (; it < nchunks; ++it) {
-        const int s = it & 1, c = chunk_of(it), L = chunk_len(c);
-        BtStage& st = sm.st[s];
-        if (it >= 2 && !(ok = tc::mbar_wait(&sm.empty[s], ((it >> 1) - 1) & 1))) break;
+    }
+    int it = 0;
+    for (; it < nchunks; ++it) {
+      const int s = it & 1, c = chunk_of(it), L = chunk_len(c);
+      BtStage& st = sm.st[s];
+      if (it >= 2 && !(ok = warp_wait(&sm.empty[s], ((it >> 1) - 1) & 1))) break;
+      if (lane == 0) {
         const int64_t t0 = bos + (int64_t)c * kChunk;
         const int tt = (int)t0, hh = (int)h;
         tc::mbar_arrive_expect_tx(&sm.full[s], kStageTx);
@@ -670,9 +702,13 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
         tc::tma_load_3d(st.Aqk, &tmA, &sm.full[s], 0, hh, tt);
         tc::bulk_load(st.glast, ws.G + ((t0 + L - 1) * H + h) * kTcK, kTcK * 4, &sm.full[s]);
       }
-      for (int j = (it < 2 ? 0 : it - 2); j < it; ++j)
-        if (!tc::mbar_wait(&sm.full[j & 1], (j >> 1) & 1)) ok = false;
+      __syncwarp();
+      if (!(ok = warp_wait(&sm.full[s], (it >> 1) & 1))) break;
+#pragma unroll
+      for (int j = 0; j < kTcK / 32; ++j) st.D[lane + 32 * j] = exp2_approx(st.glast[lane + 32 * j]);
+      tc::mbar_arrive(&sm.dready[s]);
     }
+    if (!ok && it < nchunks) tc::mbar_wait(&sm.full[it & 1], (it >> 1) & 1);
   } else {
     // ------------------------------------------------------------ output writer
     // dh^T from the dS^T operand tile, dv from its [t][v] tile.  The state
