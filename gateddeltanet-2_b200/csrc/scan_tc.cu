@@ -73,7 +73,7 @@ struct alignas(1024) TcSmem {
   __nv_bfloat16 VN[128 * 64];     // v_new^T in bf16, [v][t]
   __nv_bfloat16 OT[2][64 * 64];   // o in bf16, [t][v], two 64-column blocks
   uint64_t full[2], empty[2], dready[2];
-  uint64_t sa_ready, sa_free, mma12, vn_ready, mma34, o_full, ot_free;
+  uint64_t sa_ready, sa_free, mma12, vn_ready, vst_ready, mma34, o_full, ot_free;
   uint32_t tbase;
 };
 static_assert(sizeof(TcSmem) + 1024 <= 227 * 1024, "tcgen05 scan shared memory");
@@ -137,6 +137,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
     tc::mbar_init(&sm.sa_free, 1);
     tc::mbar_init(&sm.mma12, 1);
     tc::mbar_init(&sm.vn_ready, kStateThreads);
+    tc::mbar_init(&sm.vst_ready, kStateThreads);
     tc::mbar_init(&sm.mma34, 1);
     tc::mbar_init(&sm.o_full, kStateThreads);
     tc::mbar_init(&sm.ot_free, 1);
@@ -250,21 +251,24 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
           u[i] = vn;
           x[i] = __bfloat162float(vn);
         }
+        // the MMA operand first; the copy for the store follows off the critical path
+        char* row = reinterpret_cast<char*>(sm.VN) + v * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+        tc::fence_proxy_async();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&sm.vn_ready);
         if (kSave) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int t = tb0 + i;
             ucol[(t * 128 + ((vb ^ (t & 7)) << 4)) >> 1] = u[i];
           }
+          tc::fence_proxy_async();
         }
-        char* row = reinterpret_cast<char*>(sm.VN) + v * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+        tc::mbar_arrive(&sm.vst_ready);  // the stage's U reads (and v_new writes) are done
       }
-      tc::fence_proxy_async();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&sm.vn_ready);
 
       // the chunk's products are complete: S is updated, o is in TMEM
       if (!(ok = warp_wait(&sm.mma34, c & 1))) break;
@@ -369,7 +373,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
     // Per chunk c: h^T of c (from the S^T operand tile), o of chunk c - 1 (its
     // output step runs during chunk c), v_new of c (in place over the U tile),
     // then the releases.  Every release (sa_free, ot_free, the stage's empty)
-    // follows this warp's wait on vn_ready(c), which keeps the state warps
+    // follows this warp's wait on vst_ready(c), which keeps the state warps
     // within one phase of each barrier this warp waits on.
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.o);
     auto store_o = [&](int cc) {
@@ -403,7 +407,7 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const __grid
         if (!(ok = warp_wait(&sm.o_full, (c - 1) & 1))) break;
         store_o(c - 1);
       }
-      if (!(ok = warp_wait(&sm.vn_ready, c & 1))) break;
+      if (!(ok = warp_wait(&sm.vst_ready, c & 1))) break;
       if (kSave) {
         if (L == kChunk) {
           if (lane == 0) {
@@ -471,7 +475,7 @@ struct alignas(1024) BtSmem {
   __nv_bfloat16 DVA[128 * 64];     // -dv^T in bf16, [v][t] (A of MMA-d)
   __nv_bfloat16 DVT[2][64 * 64];   // dv in bf16, [t][v] (stored)
   uint64_t full[2], empty[2], dready[2];
-  uint64_t dsa_ready, dsa_free, dv_ready, dva_ready, dvt_free, ds_ready;
+  uint64_t dsa_ready, dsa_free, dv_ready, dva_ready, dvt_ready, dvt_free, ds_ready;
   uint32_t tbase;
 };
 static_assert(sizeof(BtSmem) + 1024 <= 227 * 1024, "tcgen05 backward scan shared memory");
@@ -510,6 +514,7 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
     tc::mbar_init(&sm.dsa_free, 1);
     tc::mbar_init(&sm.dv_ready, 1);
     tc::mbar_init(&sm.dva_ready, kStateThreads);
+    tc::mbar_init(&sm.dvt_ready, kStateThreads);
     tc::mbar_init(&sm.dvt_free, 1);
     tc::mbar_init(&sm.ds_ready, 1);
     tc::mbar_fence_init();
@@ -588,30 +593,35 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
       tc::tc_fence_before();
       tc::mbar_arrive(&sm.dsa_ready);
 
-      // step 2: dv -> stored tile [t][v] and the negated operand [v][t]
+      // step 2: dv -> the negated operand [v][t] (critical), then the stored tile [t][v]
       if (!(ok = warp_wait(&sm.dv_ready, it & 1))) break;
       tc::tc_fence_after();
       {
         float x[32];
         tc::tmem_ld32(tl + kColDV + tb0, x);
         tc::tmem_wait_ld();
-        if (it > 0 && !(ok = warp_wait(&sm.dvt_free, (it - 1) & 1))) break;
-        char* dvt = reinterpret_cast<char*>(sm.DVT[v >> 6]);
+        __nv_bfloat16 dvb[32];
+        float nx[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int t = tb0 + i;
-          const __nv_bfloat16 dvb = __float2bfloat16_rn(t < L ? x[i] : 0.f);
-          *reinterpret_cast<__nv_bfloat16*>(dvt + tc::sw128_off(t, v & 63)) = dvb;
-          x[i] = -__bfloat162float(dvb);
+          dvb[i] = __float2bfloat16_rn(tb0 + i < L ? x[i] : 0.f);
+          nx[i] = -__bfloat162float(dvb[i]);
         }
         char* row = reinterpret_cast<char*>(sm.DVA) + v * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(x + 8 * q);
+          *reinterpret_cast<uint4*>(row + (((4 * half + q) ^ (v & 7)) << 4)) = pack8(nx + 8 * q);
+        tc::fence_proxy_async();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&sm.dva_ready);
+        if (it > 0 && !(ok = warp_wait(&sm.dvt_free, (it - 1) & 1))) break;
+        char* dvt = reinterpret_cast<char*>(sm.DVT[v >> 6]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          *reinterpret_cast<__nv_bfloat16*>(dvt + tc::sw128_off(tb0 + i, v & 63)) = dvb[i];
+        tc::fence_proxy_async();
+        tc::mbar_arrive(&sm.dvt_ready);
       }
-      tc::fence_proxy_async();
-      tc::tc_fence_before();
-      tc::mbar_arrive(&sm.dva_ready);
       if (!(ok = warp_wait(&sm.ds_ready, it & 1))) break;
       tc::tc_fence_after();
     }
@@ -712,7 +722,7 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
   } else {
     // ------------------------------------------------------------ output writer
     // dh^T from the dS^T operand tile, dv from its [t][v] tile.  The state
-    // warps cannot run more than one phase of dsa_ready / dva_ready ahead of
+    // warps cannot run more than one phase of dsa_ready / dvt_ready ahead of
     // this warp (they wait for dsa_free / dvt_free before refilling the tiles).
     for (int it = 0; it < nchunks; ++it) {
       const int c = chunk_of(it), L = chunk_len(c);
@@ -727,7 +737,7 @@ chunk_scan_bwd_tc_kernel(const gdn2_chunk_args a, const gdn2_chunk_grads gr, con
         tc::mbar_arrive(&sm.dsa_free);
       }
       __syncwarp();
-      if (!(ok = warp_wait(&sm.dva_ready, it & 1))) break;
+      if (!(ok = warp_wait(&sm.dvt_ready, it & 1))) break;
       if (L == kChunk) {
         if (lane == 0) {
           tc::tma_store_3d(&tmDV, sm.DVT[0], 0, (int)h, (int)t0);
