@@ -200,6 +200,46 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&x)[32]) 
       : "memory");
 }
 
+// M = 64 accumulators (cta_group::1) keep row m in TMEM lane 32 (m / 16) + m % 16;
+// warp w reads rows [16 (w % 4), 16 (w % 4) + 16) of its lane quarter.  The
+// 16x256b shape hands each thread exactly the m16n8 accumulator fragment of
+// mma.sync: per 8-column group j, registers {4j, 4j+1} = row g, columns 2t, 2t+1
+// and {4j+2, 4j+3} = row g + 8 (g = lane / 4, t = lane % 4).  NF groups of 8
+// columns starting at the address's column.
+template <int NF>
+__device__ __forceinline__ void tmem_ld_frag(uint32_t taddr, float (*f)[4]);
+
+template <>
+__device__ __forceinline__ void tmem_ld_frag<2>(uint32_t taddr, float (*f)[4]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i >> 2][i & 3] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld_frag<4>(uint32_t taddr, float (*f)[4]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) f[i >> 2][i & 3] = __uint_as_float(r[i]);
+}
+
+// any even number of groups, as loads of 4 and 2 groups (8 columns each)
+template <int NF>
+__device__ __forceinline__ void tmem_ld_frag(uint32_t taddr, float (*f)[4]) {
+  static_assert(NF % 2 == 0 && NF > 4, "even group count");
+  tmem_ld_frag<4>(taddr, f);
+  tmem_ld_frag<NF - 4>(taddr + 32, f + 4);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
