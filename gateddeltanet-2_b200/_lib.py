@@ -25,6 +25,7 @@ TRANSPOSE_STATE = 1 << 3
 HAS_H0 = 1 << 4
 STORE_FINAL = 1 << 5
 SAVE_FOR_BWD = 1 << 6
+BWD_STATE_ONLY = 1 << 7
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -79,6 +80,7 @@ _lib = None
 EXPORTS = (
     "gdn2_chunk_workspace_size", "gdn2_chunk_bwd_workspace_size", "gdn2_chunk_fwd",
     "gdn2_chunk_bwd", "gdn2_recurrent_fwd", "gdn2_cp_transition", "gdn2_cp_compose",
+    "gdn2_cp_compose_bwd",
     "gdn2_status_string", "gdn2_device_supported", "gdn2_abi_version",
     "gdn2_profile_enable", "gdn2_profile_read", "gdn2_device_fault_read",
 )
@@ -109,6 +111,8 @@ def load() -> ctypes.CDLL:
     lib.gdn2_cp_transition.restype = ctypes.c_int
     lib.gdn2_cp_compose.argtypes = [_p, _i32, _i64, _i64, _i64, _i64, _p, _p]
     lib.gdn2_cp_compose.restype = ctypes.c_int
+    lib.gdn2_cp_compose_bwd.argtypes = [_p, _p, _i32, _i32, _i64, _i64, _i64, _i64, _p, _p]
+    lib.gdn2_cp_compose_bwd.restype = ctypes.c_int
     lib.gdn2_status_string.argtypes = [ctypes.c_int]
     lib.gdn2_status_string.restype = ctypes.c_char_p
     lib.gdn2_device_supported.argtypes = [ctypes.c_int]

@@ -58,93 +58,91 @@ def _make_args(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, ht, o, fl
     )
 
 
-class ChunkGDN2Function(torch.autograd.Function):
-    """Autograd wrapper; forward signature as the reference's
-    ``ChunkGDN2Function.forward`` (``chunk_gdn2.py:2515-2536``)."""
+def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, output_final_state,
+                   use_qk_l2norm_in_kernel, use_gate_in_kernel, cu_seqlens, cu_seqlens_cpu,
+                   lower_bound, transpose_state_layout, save):
+    """One ``gdn2_chunk_fwd`` call.  Returns (o, ht, saved, meta, ws, args):
+    ``saved`` and ``meta`` are what ``_chunk_backward`` needs (``save`` keeps
+    the backward's operands in the workspace)."""
+    _lib.require_device(q)
+    dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, b.dtype, w.dtype)
+    bw = _bw_dtype(b, w)
+    qb, kb, vb = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
+    gf = g.to(torch.float32).contiguous()
+    bb, wb = b.to(bw).contiguous(), w.to(bw).contiguous()
+    A_log_f = A_log.float().contiguous() if (use_gate_in_kernel and A_log is not None) else None
+    dt_f = dt_bias.float().contiguous() if (use_gate_in_kernel and dt_bias is not None) else None
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    if cu_seqlens is not None:
+        cu = cu_seqlens.to(torch.int64).contiguous()
+        cidx, coff, NT = prepare_chunk_indices(cu, cu_seqlens_cpu)
+        N = len(cu_seqlens) - 1
+    else:
+        cu = cidx = coff = None
+        N = B
+        NT = B * ((T + CHUNK - 1) // CHUNK)
+    geom = (cu, cidx, coff, N, NT)
+    flags = 0
+    if use_qk_l2norm_in_kernel:
+        flags |= _lib.L2NORM_QK
+    if use_gate_in_kernel:
+        flags |= _lib.GATE_IN_KERNEL
+        if lower_bound is not None:
+            flags |= _lib.LOWER_BOUND
+    if transpose_state_layout:
+        flags |= _lib.TRANSPOSE_STATE
+    h0 = None
+    if initial_state is not None:
+        h0 = initial_state.contiguous()
+        flags |= _lib.HAS_H0
+    if save:
+        flags |= _lib.SAVE_FOR_BWD
+    o = torch.empty(B, T, H, V, device=q.device, dtype=torch.bfloat16)
+    ht = None
+    if output_final_state:
+        shp = (N, H, V, K) if transpose_state_layout else (N, H, K, V)
+        ht = torch.empty(shp, device=q.device, dtype=torch.float32)
+        flags |= _lib.STORE_FINAL
+    lb = lower_bound if (flags & _lib.LOWER_BOUND) else None
+    args = _make_args(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, scale, h0, ht, o, flags, lb, geom)
+    lib = _lib.load()
+    ws_bytes = lib.gdn2_chunk_workspace_size(args)
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        _lib.check(lib.gdn2_chunk_fwd(args, ws.data_ptr(), ws_bytes, _lib.stream_ptr(q.device)),
+                   "gdn2_chunk_fwd")
+    o_out = o if dtypes[0] == torch.bfloat16 else o.to(dtypes[0])
+    saved = (qb, kb, vb, gf, bb, wb, A_log_f, dt_f, h0, ws, cu, cidx, coff)
+    meta = (flags, float(scale), lb, N, NT, ws_bytes, dtypes,
+            A_log.dtype if A_log is not None else None,
+            dt_bias.dtype if dt_bias is not None else None,
+            initial_state is not None)
+    return o_out, ht, saved, meta, ws, args
 
-    @staticmethod
-    def forward(ctx, q, k, v, g, b, w, A_log, dt_bias, scale, initial_state,
-                output_final_state, use_qk_l2norm_in_kernel, use_gate_in_kernel,
-                cu_seqlens, cu_seqlens_cpu, safe_gate, lower_bound, disable_recompute,
-                return_intermediate_states, transpose_state_layout):
-        _lib.require_device(q)
-        dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, b.dtype, w.dtype)
-        bw = _bw_dtype(b, w)
-        qb, kb, vb = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-        gf = g.to(torch.float32).contiguous()
-        bb, wb = b.to(bw).contiguous(), w.to(bw).contiguous()
-        A_log_f = A_log.float().contiguous() if (use_gate_in_kernel and A_log is not None) else None
-        dt_f = dt_bias.float().contiguous() if (use_gate_in_kernel and dt_bias is not None) else None
-        B, T, H, K = q.shape
-        V = v.shape[-1]
-        if cu_seqlens is not None:
-            cu = cu_seqlens.to(torch.int64).contiguous()
-            cidx, coff, NT = prepare_chunk_indices(cu, cu_seqlens_cpu)
-            N = len(cu_seqlens) - 1
-        else:
-            cu = cidx = coff = None
-            N = B
-            NT = B * ((T + CHUNK - 1) // CHUNK)
-        geom = (cu, cidx, coff, N, NT)
 
-        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
-        save = need_grad or return_intermediate_states
-        flags = 0
-        if use_qk_l2norm_in_kernel:
-            flags |= _lib.L2NORM_QK
-        if use_gate_in_kernel:
-            flags |= _lib.GATE_IN_KERNEL
-            if lower_bound is not None:
-                flags |= _lib.LOWER_BOUND
-        if transpose_state_layout:
-            flags |= _lib.TRANSPOSE_STATE
-        h0 = None
-        if initial_state is not None:
-            h0 = initial_state.contiguous()
-            flags |= _lib.HAS_H0
-        if save:
-            flags |= _lib.SAVE_FOR_BWD
-        o = torch.empty(B, T, H, V, device=q.device, dtype=torch.bfloat16)
-        ht = None
-        if output_final_state:
-            shp = (N, H, V, K) if transpose_state_layout else (N, H, K, V)
-            ht = torch.empty(shp, device=q.device, dtype=torch.float32)
-            flags |= _lib.STORE_FINAL
-        lb = lower_bound if (flags & _lib.LOWER_BOUND) else None
-        args = _make_args(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, scale, h0, ht, o, flags, lb, geom)
-        lib = _lib.load()
-        ws_bytes = lib.gdn2_chunk_workspace_size(args)
-        ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
-        with torch.cuda.device(q.device):
-            _lib.check(lib.gdn2_chunk_fwd(args, ws.data_ptr(), ws_bytes, _lib.stream_ptr(q.device)),
-                       "gdn2_chunk_fwd")
-        o_out = o if dtypes[0] == torch.bfloat16 else o.to(dtypes[0])
-
-        if return_intermediate_states:
-            assert torch.is_inference_mode_enabled(), (
-                "return_intermediate_states is only allowed in inference mode")
-            h = _intermediate_states(ws, args, B, T, H, K, V, NT, transpose_state_layout)
-            return o_out, ht, h
-
-        ctx.save_for_backward(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, h0, ws, cu, cidx, coff)
-        ctx.meta = (flags, float(scale), lb, N, NT, ws_bytes, dtypes,
-                    A_log.dtype if A_log is not None else None,
-                    dt_bias.dtype if dt_bias is not None else None,
-                    initial_state is not None)
-        return o_out, ht
-
-    @staticmethod
-    def backward(ctx, do, dht):
-        (qb, kb, vb, gf, bb, wb, A_log_f, dt_f, h0, ws, cu, cidx, coff) = ctx.saved_tensors
-        (flags, scale, lb, N, NT, ws_bytes, dtypes, A_dtype, dt_dtype, has_h0) = ctx.meta
-        B, T, H, K = qb.shape
-        V = vb.shape[-1]
-        dev = qb.device
-        geom = (cu, cidx, coff, N, NT)
-        args = _make_args(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, scale, h0, None, None,
-                          flags & ~_lib.STORE_FINAL, lb, geom)
-        dob = do.to(torch.bfloat16).contiguous()
-        dht_f = dht.to(torch.float32).contiguous() if dht is not None else None
+def _chunk_backward(saved, meta, do, dht, state_only=False):
+    """One ``gdn2_chunk_bwd`` call on a forward's saved state.  Returns the
+    gradient tuple of ``ChunkGDN2Function.backward`` or, with ``state_only``,
+    only d(loss)/d(initial state) for the given do and dht (the state-cotangent
+    scan alone; the initial state's layout follows the forward's)."""
+    (qb, kb, vb, gf, bb, wb, A_log_f, dt_f, h0, ws, cu, cidx, coff) = saved
+    (flags, scale, lb, N, NT, ws_bytes, dtypes, A_dtype, dt_dtype, has_h0) = meta
+    B, T, H, K = qb.shape
+    V = vb.shape[-1]
+    dev = qb.device
+    geom = (cu, cidx, coff, N, NT)
+    bflags = flags & ~_lib.STORE_FINAL
+    if state_only:
+        bflags |= _lib.BWD_STATE_ONLY
+    args = _make_args(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, scale, h0, None, None, bflags, lb, geom)
+    dob = do.to(torch.bfloat16).contiguous()
+    dht_f = dht.to(torch.float32).contiguous() if dht is not None else None
+    tr = bool(flags & _lib.TRANSPOSE_STATE)
+    if state_only:
+        dh0 = torch.empty((N, H, V, K) if tr else (N, H, K, V), device=dev, dtype=torch.float32)
+        grads = _lib.ChunkGrads(dout=_lib.ptr(dob), dht=_lib.ptr(dht_f), dh0=_lib.ptr(dh0))
+    else:
         dq = torch.empty_like(qb)
         dk = torch.empty_like(kb)
         dv = torch.empty_like(vb)
@@ -159,17 +157,49 @@ class ChunkGDN2Function(torch.autograd.Function):
             dout=_lib.ptr(dob), dht=_lib.ptr(dht_f), dq=_lib.ptr(dq), dk=_lib.ptr(dk),
             dv=_lib.ptr(dv), dg=_lib.ptr(dg), db=_lib.ptr(db), dw=_lib.ptr(dw),
             dh0=_lib.ptr(dh0), dA_log=_lib.ptr(dA), ddt_bias=_lib.ptr(ddt))
-        lib = _lib.load()
-        bws_bytes = lib.gdn2_chunk_bwd_workspace_size(args)
-        bws = torch.empty(max(bws_bytes, 1), device=dev, dtype=torch.uint8)
-        with torch.cuda.device(dev):
-            _lib.check(lib.gdn2_chunk_bwd(args, grads, ws.data_ptr(), ws_bytes, bws.data_ptr(),
-                                          bws_bytes, _lib.stream_ptr(dev)), "gdn2_chunk_bwd")
-        qd, kd, vd, gd, bd, wd = dtypes
-        return (dq.to(qd), dk.to(kd), dv.to(vd), dg.to(gd), db.to(bd), dw.to(wd),
-                dA.to(A_dtype) if dA is not None else None,
-                ddt.to(dt_dtype) if ddt is not None else None,
-                None, dh0, None, None, None, None, None, None, None, None, None, None)
+    lib = _lib.load()
+    bws_bytes = lib.gdn2_chunk_bwd_workspace_size(args)
+    bws = torch.empty(max(bws_bytes, 1), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        _lib.check(lib.gdn2_chunk_bwd(args, grads, ws.data_ptr(), ws_bytes, bws.data_ptr(),
+                                      bws_bytes, _lib.stream_ptr(dev)), "gdn2_chunk_bwd")
+    if state_only:
+        return dh0
+    qd, kd, vd, gd, bd, wd = dtypes
+    return (dq.to(qd), dk.to(kd), dv.to(vd), dg.to(gd), db.to(bd), dw.to(wd),
+            dA.to(A_dtype) if dA is not None else None,
+            ddt.to(dt_dtype) if ddt is not None else None,
+            dh0)
+
+
+class ChunkGDN2Function(torch.autograd.Function):
+    """Autograd wrapper; forward signature as the reference's
+    ``ChunkGDN2Function.forward`` (``chunk_gdn2.py:2515-2536``)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, A_log, dt_bias, scale, initial_state,
+                output_final_state, use_qk_l2norm_in_kernel, use_gate_in_kernel,
+                cu_seqlens, cu_seqlens_cpu, safe_gate, lower_bound, disable_recompute,
+                return_intermediate_states, transpose_state_layout):
+        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
+        o_out, ht, saved, meta, ws, args = _chunk_forward(
+            q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, output_final_state,
+            use_qk_l2norm_in_kernel, use_gate_in_kernel, cu_seqlens, cu_seqlens_cpu, lower_bound,
+            transpose_state_layout, need_grad or return_intermediate_states)
+        if return_intermediate_states:
+            assert torch.is_inference_mode_enabled(), (
+                "return_intermediate_states is only allowed in inference mode")
+            B, T, H, K = q.shape
+            h = _intermediate_states(ws, args, B, T, H, K, v.shape[-1], meta[4], transpose_state_layout)
+            return o_out, ht, h
+        ctx.save_for_backward(*saved)
+        ctx.meta = meta
+        return o_out, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        g = _chunk_backward(ctx.saved_tensors, ctx.meta, do, dht)
+        return g[:8] + (None, g[8], None, None, None, None, None, None, None, None, None, None)
 
 
 def _intermediate_states(ws, args, B, T, H, K, V, NT, transpose):

@@ -12,6 +12,16 @@ Protocol (forward, inference/prefill):
 4. each rank runs the ordinary chunked forward on its shard from that state
    (the "correction pass"), which yields its outputs and exit state.
 
+Backward (training): the cotangent of a shard's exit state maps to that of
+its entering state affinely, ``dS_in = M^T dS_out + g`` with ``g`` this
+shard's own contribution (the state-cotangent scan alone, ``dS_out`` = the
+shard's own ``dht``).  One ``all_gather`` of the ``g`` (``[N, H, K, V]`` fp32
+per rank); each rank folds the ranks after it into the cotangent of its exit
+state (``gdn2_cp_compose_bwd``) and runs the ordinary backward of its shard
+with it.  The gradient of the sequence's initial state is rank 0's.  The maps
+only parallelise the forward: the gradients are those of the sequential
+computation.
+
 The reference implements this scheme for KDA only
 (``lit_gpt/gdn2_ops/chunk_kda.py:774-945``); ``chunk_gdn2`` never passes a
 context-parallel context.  The steps are pluggable (``backend``) so the
@@ -24,7 +34,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .chunk import chunk_gdn2
+from .chunk import _chunk_backward, _chunk_forward, chunk_gdn2
 
 
 class CudaBackend:
@@ -79,12 +89,88 @@ class CudaBackend:
             return chunk_gdn2(q, k, v, g, b, w, initial_state=initial_state,
                               output_final_state=True, **kw)
 
+    # ---- training pieces -------------------------------------------------
+    def forward_train(self, q, k, v, g, b, w, *, initial_state, scale, use_qk_l2norm_in_kernel,
+                      use_gate_in_kernel, A_log, dt_bias, lower_bound):
+        """The shard's forward from ``initial_state``, keeping its backward operands."""
+        o, ht, saved, meta, _, _ = _chunk_forward(
+            q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, True, use_qk_l2norm_in_kernel,
+            use_gate_in_kernel, None, None, lower_bound, False, True)
+        return o, ht, (saved, meta)
+
+    def state_cotangent(self, data, do, dht):
+        """d(loss)/d(entering state) of the shard alone, for its do and dht."""
+        return _chunk_backward(data[0], data[1], do, dht, state_only=True)
+
+    def compose_bwd(self, gathered_maps, gathered_g, rank, dht):
+        W, N, H, K, _ = gathered_maps.shape
+        V = gathered_g.shape[-1]
+        out = dht.to(torch.float32).contiguous().clone()
+        with torch.cuda.device(out.device):
+            _lib.check(_lib.load().gdn2_cp_compose_bwd(
+                gathered_maps.contiguous().data_ptr(), gathered_g.contiguous().data_ptr(), rank, W,
+                N, H, K, V, out.data_ptr(), _lib.stream_ptr(out.device)), "gdn2_cp_compose_bwd")
+        return out
+
+    def backward(self, data, do, dS_out):
+        """(dq, dk, dv, dg, db, dw, dA_log, ddt_bias, d entering state) of the shard."""
+        return _chunk_backward(data[0], data[1], do, dS_out)
+
+
+def _gather(x, group, world):
+    if world == 1:
+        return x.unsqueeze(0)
+    flat = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(flat, x.contiguous(), group=group)
+    return flat.view((world,) + tuple(x.shape))
+
+
+class ChunkGDN2CPFunction(torch.autograd.Function):
+    """Autograd of the context-parallel op (see the module docstring)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, b, w, A_log, dt_bias, initial_state, scale, use_qk_l2norm_in_kernel,
+                use_gate_in_kernel, lower_bound, group, backend):
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        B, T, H, K = q.shape
+        V = v.shape[-1]
+        kw = dict(use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel, use_gate_in_kernel=use_gate_in_kernel,
+                  A_log=A_log, dt_bias=dt_bias, lower_bound=lower_bound)
+        maps = backend.transition(q, k, v, g, b, w, scale=scale, **kw)
+        gathered = _gather(maps, group, world)
+        if initial_state is None:
+            state = torch.zeros(B, H, K, V, dtype=maps.dtype, device=maps.device)
+        else:
+            state = initial_state.to(device=maps.device, dtype=maps.dtype)
+        S_in = backend.compose(gathered, rank, state)
+        o, ht, data = backend.forward_train(q, k, v, g, b, w, initial_state=S_in, scale=scale, **kw)
+        ctx.data, ctx.gathered = data, gathered
+        ctx.cp = (rank, world, group, backend, initial_state is not None, ht.shape, ht.dtype)
+        return o, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        rank, world, group, backend, has_h0, ht_shape, ht_dtype = ctx.cp
+        if dht is None:
+            dht = torch.zeros(ht_shape, dtype=ht_dtype, device=do.device)
+        gp = backend.state_cotangent(ctx.data, do, dht)
+        gathered_g = _gather(gp, group, world)
+        dS_out = backend.compose_bwd(ctx.gathered, gathered_g, rank, dht)
+        dq, dk, dv, dg, db, dw, dA, ddt, dS_in = backend.backward(ctx.data, do, dS_out)
+        dh0 = None
+        if has_h0:
+            dh0 = dS_in if rank == 0 else torch.zeros_like(dS_in)
+        return dq, dk, dv, dg, db, dw, dA, ddt, dh0, None, None, None, None, None, None
+
 
 def chunk_gdn2_cp(q, k, v, g, b, w, *, group=None, scale=None, initial_state=None,
                   use_qk_l2norm_in_kernel=False, use_gate_in_kernel=False, A_log=None,
                   dt_bias=None, lower_bound=None, backend=None):
-    """Forward of ``chunk_gdn2`` for a sequence whose T axis is sharded over
-    ``group`` (this rank holds shard ``rank``; all shards have equal length).
+    """``chunk_gdn2`` for a sequence whose T axis is sharded over ``group``
+    (this rank holds shard ``rank``; all shards have equal length).  With
+    inputs that require grad the result is differentiable (every rank must
+    run the backward: it holds one all_gather).
 
     q, k, g, b: ``[B, T_shard, H, K]``; v, w: ``[B, T_shard, H, V]``;
     ``initial_state``: the sequence's initial state ``[B, H, K, V]`` fp32 (read
@@ -92,6 +178,13 @@ def chunk_gdn2_cp(q, k, v, g, b, w, *, group=None, scale=None, initial_state=Non
     rank's exit state is the sequence's final state.
     """
     backend = backend or CudaBackend()
+    if scale is None:
+        scale = q.shape[-1] ** -0.5
+    inputs = (q, k, v, g, b, w, A_log, dt_bias, initial_state)
+    if torch.is_grad_enabled() and any(x is not None and x.requires_grad for x in inputs):
+        return ChunkGDN2CPFunction.apply(q, k, v, g, b, w, A_log, dt_bias, initial_state, scale,
+                                         use_qk_l2norm_in_kernel, use_gate_in_kernel, lower_bound,
+                                         group, backend)
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     B, T, H, K = q.shape

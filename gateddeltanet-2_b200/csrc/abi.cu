@@ -101,11 +101,14 @@ int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr, const v
   int st = check_chunk(a, true, false);  // the backward reads no o / ht
   if (st) return st;
   if (!(a->flags & GDN2_SAVE_FOR_BWD)) return GDN2_ERR_FLAGS;
-  if (!gr || !gr->dout || !gr->dq || !gr->dk || !gr->dv || !gr->dg || !gr->db || !gr->dw)
+  const bool state_only = a->flags & GDN2_BWD_STATE_ONLY;
+  if (!gr || !gr->dout) return GDN2_ERR_NULL_POINTER;
+  if (state_only ? !gr->dh0 : (!gr->dq || !gr->dk || !gr->dv || !gr->dg || !gr->db || !gr->dw))
     return GDN2_ERR_NULL_POINTER;
   if ((a->flags & GDN2_HAS_H0) && !gr->dh0) return GDN2_ERR_NULL_POINTER;
-  if ((a->flags & GDN2_GATE_IN_KERNEL) && !gr->dA_log) return GDN2_ERR_NULL_POINTER;
-  if ((a->flags & GDN2_GATE_IN_KERNEL) && a->dt_bias && !gr->ddt_bias) return GDN2_ERR_NULL_POINTER;
+  if (!state_only && (a->flags & GDN2_GATE_IN_KERNEL) && !gr->dA_log) return GDN2_ERR_NULL_POINTER;
+  if (!state_only && (a->flags & GDN2_GATE_IN_KERNEL) && a->dt_bias && !gr->ddt_bias)
+    return GDN2_ERR_NULL_POINTER;
   const size_t need = chunk_ws_layout(*a, nullptr, nullptr);
   if (need > workspace_bytes || (need > 0 && !workspace)) return GDN2_ERR_WORKSPACE;
   const size_t need_b = bwd_ws_layout(*a, nullptr, nullptr);

@@ -863,6 +863,7 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
     chunk_scan_bwd_kernel<K, V><<<g2, kBScanThreads, sm2, s>>>(a, g, ws, bw);
     GDN2_LAUNCH_CHECK();
   }
+  if (a.flags & GDN2_BWD_STATE_ONLY) return 0;
   if (a.NT > 0) {
     const bool bwb = a.dtype_bw == GDN2_BF16;
     const size_t sm3 = bwb ? sizeof(BIntraSmem<K, V, __nv_bfloat16>) : sizeof(BIntraSmem<K, V, float>);

@@ -64,6 +64,51 @@ cp_compose_kernel(const float* __restrict__ maps, int rank, int64_t NH, int64_t 
   }
 }
 
+// Backward fold over the ranks after `rank`, one CTA per (sequence x head,
+// 32-column tile): X <- M_j^T X + g_j for j = world-1 .. rank+1 (X = 0 first),
+// then dstate += X.
+template <int K>
+__global__ void __launch_bounds__(kComposeThreads)
+cp_compose_bwd_kernel(const float* __restrict__ maps, const float* __restrict__ gs, int rank, int world, int64_t NH,
+                      int64_t V, float* __restrict__ dstate) {
+  extern __shared__ float cp_smem[];
+  float (*Mt)[K + 1] = reinterpret_cast<float (*)[K + 1]>(cp_smem);  // Mt[x][r] = M[r][x]
+  float (*Xs)[kComposeBV + 1] = reinterpret_cast<float (*)[kComposeBV + 1]>(cp_smem + K * (K + 1));
+  const int tid = threadIdx.x;
+  const int64_t nh = blockIdx.y;
+  const int v0 = blockIdx.x * kComposeBV;
+  const int64_t W = K + V;
+  for (int i = tid; i < K * kComposeBV; i += kComposeThreads) Xs[i / kComposeBV][i % kComposeBV] = 0.f;
+  constexpr int kPer = K * kComposeBV / kComposeThreads;
+  for (int j = world - 1; j > rank; --j) {
+    const float* mp = maps + ((int64_t)j * NH + nh) * K * W;
+    const float* gp = gs + ((int64_t)j * NH + nh) * K * V;
+    __syncthreads();
+    for (int i = tid; i < K * K; i += kComposeThreads) Mt[i % K][i / K] = mp[(int64_t)(i / K) * W + (i % K)];
+    __syncthreads();
+    float out[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * kComposeThreads, r = i / kComposeBV, c = i % kComposeBV;
+      float acc = gp[(int64_t)r * V + v0 + c];
+      for (int x = 0; x < K; ++x) acc = fmaf(Mt[r][x], Xs[x][c], acc);
+      out[u] = acc;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = tid + u * kComposeThreads;
+      Xs[i / kComposeBV][i % kComposeBV] = out[u];
+    }
+  }
+  __syncthreads();
+  float* st = dstate + nh * (int64_t)K * V;
+  for (int i = tid; i < K * kComposeBV; i += kComposeThreads) {
+    const int r = i / kComposeBV, c = i % kComposeBV;
+    st[(int64_t)r * V + v0 + c] += Xs[r][c];
+  }
+}
+
 bool dim_ok(int64_t d) { return d == 64 || d == 128; }
 
 }  // namespace
@@ -110,6 +155,31 @@ extern "C" int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t
   } else {
     const int sm = (64 * 65 + 64 * (kComposeBV + 1)) * 4;
     cp_compose_kernel<64><<<grid, kComposeThreads, sm, s>>>(gathered_maps, rank, N * H, V, state);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : -static_cast<int>(e);
+}
+
+extern "C" int gdn2_cp_compose_bwd(const float* gathered_maps, const float* gathered_g, int32_t rank, int32_t world,
+                                   int64_t N, int64_t H, int64_t K, int64_t V, float* dstate, gdn2_stream_t stream) {
+  if (!gathered_maps || !gathered_g || !dstate) return GDN2_ERR_NULL_POINTER;
+  if (rank < 0 || world <= rank || N < 0 || H <= 0) return GDN2_ERR_SHAPE;
+  if (!dim_ok(K) || !dim_ok(V)) return GDN2_ERR_UNSUPPORTED_DIM;
+  if (rank == world - 1 || N == 0) return GDN2_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)(V / kComposeBV), (unsigned)(N * H));
+  ProfScope ps(kKCp, s);
+  if (K == 128) {
+    const int sm = (128 * 129 + 128 * (kComposeBV + 1)) * 4;
+    cudaError_t e =
+        cudaFuncSetAttribute(cp_compose_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+    cp_compose_bwd_kernel<128><<<grid, kComposeThreads, sm, s>>>(gathered_maps, gathered_g, rank, world, N * H,
+                                                                 V, dstate);
+  } else {
+    const int sm = (64 * 65 + 64 * (kComposeBV + 1)) * 4;
+    cp_compose_bwd_kernel<64><<<grid, kComposeThreads, sm, s>>>(gathered_maps, gathered_g, rank, world, N * H, V,
+                                                                dstate);
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : -static_cast<int>(e);

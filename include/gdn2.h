@@ -53,7 +53,10 @@ enum gdn2_flags {
   GDN2_TRANSPOSE_STATE = 1 << 3, /* states stored [.., V, K] */
   GDN2_HAS_H0 = 1 << 4,          /* initial_state given */
   GDN2_STORE_FINAL = 1 << 5,     /* write the final state to `ht` */
-  GDN2_SAVE_FOR_BWD = 1 << 6     /* chunk fwd: keep what gdn2_chunk_bwd needs in the workspace */
+  GDN2_SAVE_FOR_BWD = 1 << 6,    /* chunk fwd: keep what gdn2_chunk_bwd needs in the workspace */
+  GDN2_BWD_STATE_ONLY = 1 << 7   /* chunk bwd: only the state-cotangent scan (no reference counterpart):
+                                    writes dh0 = d(loss)/d(initial state) for the given do and dht;
+                                    dq, dk, dv, dg, db, dw may be NULL */
 };
 
 /* status codes (> 0: invalid argument) */
@@ -221,6 +224,18 @@ int gdn2_cp_transition(const gdn2_chunk_args* a, float* maps, void* workspace,
                        size_t workspace_bytes, gdn2_stream_t stream);
 int gdn2_cp_compose(const float* gathered_maps, int32_t rank, int64_t N, int64_t H, int64_t K,
                     int64_t V, float* state, gdn2_stream_t stream);
+/* Context-parallel backward (no reference counterpart for GDN2; the reference
+ * sketches the KDA equivalent, chunk_kda.py:855-945).  Rank j's shard maps the
+ * cotangent of its exit state to that of its entering state affinely,
+ * dS_in = M_j^T dS_out + g_j, where g_j is gdn2_chunk_bwd's dh0 under
+ * GDN2_BWD_STATE_ONLY with the shard's own do and dht.  gdn2_cp_compose_bwd
+ * folds the ranks after this one: on entry `dstate` [N, H, K, V] holds this
+ * rank's own dht (or zeros); on return the full cotangent of its exit state,
+ * dht + dS_in(rank + 1) with dS_in(j) = M_j^T dS_in(j + 1) + g_j, dS_in(world) = 0.
+ * gathered_maps: [world, N, H, K, K+V] (M in columns 0..K-1, as
+ * gdn2_cp_transition writes them); gathered_g: [world, N, H, K, V]. */
+int gdn2_cp_compose_bwd(const float* gathered_maps, const float* gathered_g, int32_t rank, int32_t world,
+                        int64_t N, int64_t H, int64_t K, int64_t V, float* dstate, gdn2_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* opt-in per-kernel timing (measurement hook, no reference counterpart)     */

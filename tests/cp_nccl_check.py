@@ -42,6 +42,23 @@ def main():
     assert_close(o, o_ref[:, rank * Ts:(rank + 1) * Ts], f"o rank {rank}")
     if rank == world - 1:
         assert_close(ht, ht_ref, "final state")
+    # backward: per-shard gradients against the single-GPU backward of the sequence
+    do = (torch.randn(1, T, H, V, generator=gen) * 0.5).bfloat16().to(dev)
+    dht = (torch.randn(1, H, K, V, generator=gen) * 0.1).to(dev)
+    leaves = [x.clone().requires_grad_(True) for x in shard]
+    h0l = h0.to(dev).clone().requires_grad_(True)
+    o, ht = cp.chunk_gdn2_cp(*leaves, initial_state=h0l)
+    cot_ht = dht if rank == world - 1 else torch.zeros_like(dht)
+    torch.autograd.backward([o, ht], [do[:, rank * Ts:(rank + 1) * Ts], cot_ht])
+    full_l = [x.clone().requires_grad_(True) for x in full]
+    h0f = h0.to(dev).clone().requires_grad_(True)
+    o_f, ht_f = gdn2.chunk_gdn2(*full_l, initial_state=h0f, output_final_state=True)
+    torch.autograd.backward([o_f, ht_f], [do, dht])
+    torch.cuda.synchronize()
+    for n, lf, ls in zip("qkvgbw", full_l, leaves):
+        assert_close(ls.grad, lf.grad[:, rank * Ts:(rank + 1) * Ts], f"d{n} rank {rank}")
+    if rank == 0:
+        assert_close(h0l.grad, h0f.grad, "dh0")
     ok = torch.ones(1, device=dev)
     dist.all_reduce(ok)
     if rank == 0 and int(ok.item()) == world:
