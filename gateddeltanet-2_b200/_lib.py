@@ -66,6 +66,24 @@ class RecurrentArgs(ctypes.Structure):
     ]
 
 
+class PrepArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", _i64), ("T", _i64), ("N", _i64), ("cu_seqlens", _p),
+        ("Dk", _i64), ("Dv", _i64), ("Dfg", _i64), ("conv_size", _i64), ("proj_stride", _i64),
+        ("b_scale", _f32), ("flags", _i32),
+        ("proj", _p), ("conv_weight", _p), ("conv_bias", _p),
+        ("conv_state_in", _p), ("conv_state_out", _p),
+        ("q", _p), ("k", _p), ("v", _p), ("b", _p), ("w", _p), ("f0", _p), ("g0", _p),
+    ]
+
+
+class PrepGrads(ctypes.Structure):
+    _fields_ = [
+        ("dq", _p), ("dk", _p), ("dv", _p), ("db", _p), ("dw", _p), ("df0", _p), ("dg0", _p),
+        ("dproj", _p), ("dconv_weight", _p), ("dconv_bias", _p),
+    ]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("launches", _i64), ("total_ms", ctypes.c_double)]
 
@@ -83,6 +101,8 @@ EXPORTS = (
     "gdn2_cp_compose_bwd",
     "gdn2_status_string", "gdn2_device_supported", "gdn2_abi_version",
     "gdn2_profile_enable", "gdn2_profile_read", "gdn2_device_fault_read",
+    "gdn2_layer_prep_fwd", "gdn2_layer_prep_bwd_workspace_size", "gdn2_layer_prep_bwd",
+    "gdn2_norm_gate_fwd", "gdn2_norm_gate_bwd_workspace_size", "gdn2_norm_gate_bwd",
 )
 
 
@@ -125,6 +145,19 @@ def load() -> ctypes.CDLL:
     lib.gdn2_abi_version.restype = ctypes.c_int
     lib.gdn2_device_fault_read.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
     lib.gdn2_device_fault_read.restype = ctypes.c_int
+    lib.gdn2_layer_prep_fwd.argtypes = [ctypes.POINTER(PrepArgs), _p]
+    lib.gdn2_layer_prep_fwd.restype = ctypes.c_int
+    lib.gdn2_layer_prep_bwd_workspace_size.argtypes = [ctypes.POINTER(PrepArgs)]
+    lib.gdn2_layer_prep_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.gdn2_layer_prep_bwd.argtypes = [ctypes.POINTER(PrepArgs), ctypes.POINTER(PrepGrads), _p,
+                                        ctypes.c_size_t, _p]
+    lib.gdn2_layer_prep_bwd.restype = ctypes.c_int
+    lib.gdn2_norm_gate_fwd.argtypes = [_p, _p, _p, _f32, _i64, _i64, _p, _p, _p]
+    lib.gdn2_norm_gate_fwd.restype = ctypes.c_int
+    lib.gdn2_norm_gate_bwd_workspace_size.argtypes = [_i64, _i64]
+    lib.gdn2_norm_gate_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.gdn2_norm_gate_bwd.argtypes = [_p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, ctypes.c_size_t, _p]
+    lib.gdn2_norm_gate_bwd.restype = ctypes.c_int
     _lib = lib
     return lib
 

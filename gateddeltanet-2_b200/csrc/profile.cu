@@ -14,7 +14,9 @@ namespace {
 
 const char* kNames[kNumKernels] = {"chunk_intra_kernel", "chunk_scan_fwd_kernel", "chunk_scan_bwd_kernel",
                                    "chunk_bwd_intra_kernel", "recurrent_kernel", "cp_kernel",
-                                   "chunk_scan_fwd_tc_kernel", "chunk_scan_bwd_tc_kernel"};
+                                   "chunk_scan_fwd_tc_kernel", "chunk_scan_bwd_tc_kernel",
+                                   "layer_prep_fwd_kernel", "layer_prep_bwd_kernel",
+                                   "norm_gate_fwd_kernel", "norm_gate_bwd_kernel"};
 
 struct Pending {
   int id;

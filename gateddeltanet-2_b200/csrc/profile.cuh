@@ -3,7 +3,8 @@
 #include <cuda_runtime.h>
 
 namespace gdn2 {
-enum KernelId { kKIntra = 0, kKScanFwd, kKScanBwd, kKBwdIntra, kKRecurrent, kKCp, kKScanFwdTc, kKScanBwdTc, kNumKernels };
+enum KernelId { kKIntra = 0, kKScanFwd, kKScanBwd, kKBwdIntra, kKRecurrent, kKCp, kKScanFwdTc, kKScanBwdTc,
+                kKLayerPrepFwd, kKLayerPrepBwd, kKNormGateFwd, kKNormGateBwd, kNumKernels };
 bool prof_on();
 void prof_begin(int id, cudaStream_t s);
 void prof_end(int id, cudaStream_t s);

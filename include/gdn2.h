@@ -238,6 +238,76 @@ int gdn2_cp_compose_bwd(const float* gathered_maps, const float* gathered_g, int
                         int64_t N, int64_t H, int64_t K, int64_t V, float* dstate, gdn2_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* the GatedDeltaNet2 layer around the operator (lit_gpt/gdn2.py:282-464)    */
+/* ------------------------------------------------------------------------- */
+/*
+ * The layer's first-stage projections are one GEMM (gdn2.py:300-325) whose
+ * output rows hold the sections q_raw | k_raw | v_raw | b_raw | w_raw | f0 | g0
+ * (widths Dk, Dk, Dv, Dk, Dv, Dfg, Dfg) in that order.  gdn2_layer_prep_fwd
+ * turns that bf16 matrix into the operator's inputs in one pass:
+ *   q, k, v = SiLU(causal depthwise conv1d of q_raw | k_raw | v_raw), the fla
+ *             ShortConvolution of gdn2.py:342-367, or SiLU alone when
+ *             conv_size == 0 (gdn2.py:369-372);
+ *   b = b_scale * sigmoid(b_raw), w = sigmoid(w_raw)  (gdn2.py:398-399, :412-420);
+ *   f0, g0 copied out contiguous (inputs of the second-stage GEMMs).
+ * Sequences are rows of T tokens, or given by cu_seqlens [N+1] (device int64)
+ * over all rows (every sequence non-empty).  conv_state_in / conv_state_out:
+ * bf16 [N, 2Dk+Dv, W] holding each sequence's last W conv inputs, newest at
+ * index W-1 (fla's cache layout with the q, k, v channels concatenated); the
+ * first output of a sequence reads entries 1..W-1 as its history.
+ * conv_state_out may alias conv_state_in only when every sequence is one
+ * token (rows == N, the decode step).
+ * gdn2_layer_prep_bwd is the reverse pass: from the cotangents of q, k, v, b,
+ * w, f0, g0 it writes d(proj) (every section) and the conv weight / bias
+ * gradients in fp32 (reduced in a fixed order: bitwise reproducible).  The
+ * conv state carries no cotangent (it is an inference cache).
+ */
+typedef struct gdn2_prep_args {
+  int64_t rows, T, N;
+  const int64_t* cu_seqlens;
+  int64_t Dk, Dv, Dfg;          /* multiples of 8 */
+  int64_t conv_size;            /* W: 0 (no convolution), 2, 3 or 4 */
+  int64_t proj_stride;          /* elements between rows of proj, >= 3Dk+2Dv+2Dfg, multiple of 8 */
+  float b_scale;                /* erase-gate ceiling (2 with allow_neg_eigval) */
+  int32_t flags;                /* reserved: 0 */
+  const void* proj;             /* bf16 [rows, proj_stride] */
+  const float* conv_weight;     /* fp32 [2Dk+Dv, W] */
+  const float* conv_bias;       /* fp32 [2Dk+Dv] or NULL */
+  const void* conv_state_in;    /* bf16 [N, 2Dk+Dv, W] or NULL (zero history) */
+  void* conv_state_out;         /* bf16 [N, 2Dk+Dv, W] or NULL */
+  void *q, *k, *v;              /* bf16 [rows, Dk | Dk | Dv] */
+  void *b, *w;                  /* bf16 [rows, Dk | Dv] */
+  void *f0, *g0;                /* bf16 [rows, Dfg] each, or both NULL (not copied) */
+} gdn2_prep_args;
+
+typedef struct gdn2_prep_grads {
+  const void *dq, *dk, *dv, *db, *dw;  /* bf16, shapes of q, k, v, b, w */
+  const void *df0, *dg0;        /* bf16 [rows, Dfg], or NULL (zero) */
+  void* dproj;                  /* bf16 [rows, proj_stride]; columns past the sections untouched */
+  float* dconv_weight;          /* fp32 [2Dk+Dv, W] (overwritten) */
+  float* dconv_bias;            /* fp32 [2Dk+Dv] or NULL */
+} gdn2_prep_grads;
+
+int gdn2_layer_prep_fwd(const gdn2_prep_args* a, gdn2_stream_t stream);
+size_t gdn2_layer_prep_bwd_workspace_size(const gdn2_prep_args* a);
+int gdn2_layer_prep_bwd(const gdn2_prep_args* a, const gdn2_prep_grads* g, void* workspace,
+                        size_t workspace_bytes, gdn2_stream_t stream);
+
+/* Gated output norm, FusedRMSNormSwishGate of gdn2.py:462 (fla
+ * fused_norm_gate.py:35-104), per row of D:
+ *     y = x / sqrt(mean(x^2) + eps) * weight * gate * sigmoid(gate)
+ * x, gate, y: bf16 [rows, D]; weight fp32 [D]; rstd fp32 [rows] (kept for the
+ * backward); D in {64, 128, 256}.  The backward writes dx, dgate (bf16) and
+ * dweight (fp32 [D], overwritten, fixed reduction order) using a workspace of
+ * gdn2_norm_gate_bwd_workspace_size bytes. */
+int gdn2_norm_gate_fwd(const void* x, const void* gate, const float* weight, float eps, int64_t rows,
+                       int64_t D, void* y, float* rstd, gdn2_stream_t stream);
+size_t gdn2_norm_gate_bwd_workspace_size(int64_t rows, int64_t D);
+int gdn2_norm_gate_bwd(const void* dy, const void* x, const void* gate, const float* weight,
+                       const float* rstd, int64_t rows, int64_t D, void* dx, void* dgate, float* dweight,
+                       void* workspace, size_t workspace_bytes, gdn2_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
 /* opt-in per-kernel timing (measurement hook, no reference counterpart)     */
 /* ------------------------------------------------------------------------- */
 /* While enabled, every launch of the library is bracketed by CUDA events on

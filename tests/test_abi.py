@@ -84,3 +84,42 @@ def test_ops_fail_loudly_without_a_gpu(gdn2):
         gdn2.chunk_gdn2(x, x, x, x, x, x)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         gdn2.fused_recurrent_gdn2(x, x, x, x, x, x)
+
+
+def _prep(gdn2, **kw):
+    a = dict(rows=0, T=1, N=0, Dk=64, Dv=64, Dfg=64, conv_size=4, proj_stride=3 * 64 + 2 * 64 + 2 * 64,
+             b_scale=1.0, flags=0)
+    a.update(kw)
+    return gdn2._lib.PrepArgs(**a)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(Dk=60), 2), (dict(conv_size=5), 2), (dict(conv_size=1), 2), (dict(proj_stride=100), 2),
+    (dict(proj_stride=3 * 64 + 2 * 64 + 2 * 64 + 4), 2), (dict(flags=1), 7),
+    (dict(rows=10, T=3, N=3), 2), (dict(rows=8, T=4, N=2), 1),
+])
+def test_invalid_prep_args_rejected(gdn2, kw, code):
+    lib = gdn2._lib.load()
+    st = lib.gdn2_layer_prep_fwd(_prep(gdn2, **kw), None)
+    assert st == code, lib.gdn2_status_string(st)
+
+
+def test_prep_state_alias_needs_one_token_per_sequence(gdn2):
+    lib = gdn2._lib.load()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    a = _prep(gdn2, rows=8, T=4, N=2, conv_state_in=p, conv_state_out=p, proj=p, q=p, k=p, v=p, b=p, w=p,
+              conv_weight=p)
+    assert lib.gdn2_layer_prep_fwd(a, None) == 7
+    assert lib.gdn2_layer_prep_bwd_workspace_size(_prep(gdn2, rows=512, T=512, N=1)) == \
+        2 * (2 * 64 + 64) * 5 * 4  # two row tiles of 256, C conv channels, W taps + bias, fp32
+    assert lib.gdn2_layer_prep_bwd_workspace_size(_prep(gdn2, rows=512, T=512, N=1, conv_size=0)) == 0
+
+
+def test_invalid_norm_gate_args_rejected(gdn2):
+    lib = gdn2._lib.load()
+    assert lib.gdn2_norm_gate_fwd(None, None, None, 1e-5, 10, 96, None, None, None) == 4
+    assert lib.gdn2_norm_gate_fwd(None, None, None, 1e-5, 10, 128, None, None, None) == 1
+    assert lib.gdn2_norm_gate_fwd(None, None, None, 1e-5, 0, 128, None, None, None) == 0
+    assert lib.gdn2_norm_gate_bwd_workspace_size(10, 128) == 128 * 4
+    assert lib.gdn2_norm_gate_bwd_workspace_size(10 ** 6, 128) == 1184 * 128 * 4

@@ -1,0 +1,264 @@
+"""GPU parity of the GatedDeltaNet2 layer kernels and module against the CPU
+oracle (``oracle/layer_oracle.py``, pinned to fla's kernels and to the
+reference layer by ``tests/test_layer_oracle.py``).
+
+Elementwise kernels (prep, gated norm) store bf16, so they are held to the
+operator's bar plus that one rounding (at most 2^-8 relative):
+|x - ref| <= 1e-2 + (2e-3 + 2^-8)*|ref|; fp32 parameter gradients (sums over
+rows) to 1e-3 of the summed term magnitudes.  The whole layer
+composes bf16 GEMMs, bf16 activations and the operator, as the reference's
+bf16 training does, and is held to |x - ref| <= 3e-2 * max|ref| per tensor.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import case_names, load_case
+from oracle import layer_oracle as lo
+from tolerance import assert_close
+
+pytestmark = pytest.mark.gpu
+
+BF16_RTOL = 2e-3 + 2.0 ** -8  # the operator's rtol plus one bf16 rounding of the stored result
+
+
+def _close_bf16(actual, expected, name):
+    assert_close(actual, expected, name, rtol=BF16_RTOL)
+
+
+def _bf(x):
+    return torch.as_tensor(x).float().bfloat16()
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def _prep_call(gdn2, proj, Dk, Dv, Dfg, T, N, cu, W, b_scale, cw, cb, state_in, want_state=True):
+    from importlib import import_module
+    layer = import_module("gateddeltanet-2_b200.layer")
+    return layer.LayerPrepFunction.apply(proj, cw, cb, Dk, Dv, Dfg, T, N, cu, W, b_scale, state_in, want_state)
+
+
+def _oracle_prep(projn, Dk, Dv, Dfg, W, b_scale, cw, cb, state_in, cu, B, T):
+    offs = np.cumsum([0, Dk, Dk, Dv, Dk, Dv, Dfg, Dfg])
+    sec = [projn[:, offs[i]:offs[i + 1]].reshape(B, T, -1) for i in range(7)]
+    C = 2 * Dk + Dv
+    outs, zs, fss = [], [], []
+    for i, (c0, c1) in enumerate(((0, Dk), (Dk, 2 * Dk), (2 * Dk, C))):
+        if W:
+            y, fs, z = lo.short_conv_fwd(sec[i], cw[c0:c1], None if cb is None else cb[c0:c1],
+                                         None if state_in is None else state_in[:, c0:c1], cu)
+            fss.append(fs)
+        else:
+            z = sec[i]
+            y = z * lo.sigmoid(z)
+        outs.append(y)
+        zs.append(z)
+    b, w = lo.gates_fwd(sec[3], sec[4], b_scale)
+    return outs + [b, w, sec[5], sec[6]], zs, sec, (np.concatenate(fss, 1) if W else None)
+
+
+PREP_CASES = [
+    # B, T, cu_seqlens, Dk, Dv, Dfg, W, bias, state_in, pad, b_scale
+    (2, 100, None, 64, 128, 64, 4, True, False, 0, 1.0),
+    (1, 200, [0, 1, 3, 70, 200], 64, 64, 64, 4, False, True, 16, 2.0),
+    (1, 97, [0, 40, 97], 128, 128, 128, 3, True, True, 8, 1.0),
+    (3, 33, None, 64, 64, 64, 2, False, False, 0, 1.0),
+    (2, 50, None, 64, 64, 64, 0, False, False, 0, 1.0),
+    (5, 1, None, 64, 64, 64, 4, False, True, 0, 1.0),  # decode rows: one token per sequence
+]
+
+
+@pytest.mark.parametrize("case", PREP_CASES)
+def test_layer_prep_matches_oracle(gdn2, case):
+    B, T, cu, Dk, Dv, Dfg, W, bias, has_state, pad, b_scale = case
+    rows = B * T
+    N = B if cu is None else len(cu) - 1
+    if cu is not None:
+        B, T = 1, rows
+    gen = torch.Generator().manual_seed(rows + Dk + W)
+    width = 3 * Dk + 2 * Dv + 2 * Dfg
+    full = _bf(torch.randn(rows, width + pad, generator=gen) * 2)
+    proj = full[:, :width] if pad else full
+    C = 2 * Dk + Dv
+    cw = torch.randn(C, max(W, 1), generator=gen) * 0.5 if W else None
+    cb = torch.randn(C, generator=gen) * 0.1 if (bias and W) else None
+    st = _bf(torch.randn(N, C, W, generator=gen)) if (has_state and W) else None
+    cu_t = torch.tensor(cu, dtype=torch.int64).cuda() if cu is not None else None
+    proj_d = proj.cuda().requires_grad_(True)
+    cw_d = cw.cuda().requires_grad_(True) if cw is not None else None
+    cb_d = cb.cuda().requires_grad_(True) if cb is not None else None
+    outs = _prep_call(gdn2, proj_d, Dk, Dv, Dfg, T, N, cu_t, W, b_scale, cw_d, cb_d,
+                      st.cuda() if st is not None else None)
+    projn = _np(proj)
+    ref, zs, sec, ref_state = _oracle_prep(projn, Dk, Dv, Dfg, W, b_scale, None if cw is None else cw.double().numpy(),
+                                           None if cb is None else cb.double().numpy(),
+                                           None if st is None else _np(st), cu, B, T)
+    for nm, got, exp in zip(("q", "k", "v", "b", "w", "f0", "g0"), outs[:7], ref):
+        _close_bf16(got, exp.reshape(rows, -1), nm)
+    if W:
+        assert torch.equal(outs[7].cpu().float(), torch.as_tensor(ref_state).float()), "conv state"
+
+    # backward
+    cots = [_bf(torch.randn(o.shape, generator=gen)) for o in outs[:7]]
+    torch.autograd.backward(list(outs[:7]), [c.cuda() for c in cots])
+    cn = [_np(c) for c in cots]
+    exp_d = []
+    for i in range(3):
+        d = cn[i].reshape(B, T, -1)
+        if W:
+            c0 = (0, Dk, 2 * Dk)[i]
+            c1 = c0 + (Dk, Dk, Dv)[i]
+            dx, dwt, dbt, _ = lo.short_conv_bwd(sec[i], cw.double().numpy()[c0:c1], zs[i], d,
+                                                None if st is None else _np(st)[:, c0:c1], cu)
+            exp_d.append(dx)
+        else:
+            s = lo.sigmoid(zs[i])
+            exp_d.append(d * s * (1 + zs[i] * (1 - s)))
+    db_, dw_ = lo.gates_bwd(sec[3], sec[4], cn[3].reshape(B, T, -1), cn[4].reshape(B, T, -1), b_scale)
+    exp_d += [db_, dw_, cn[5].reshape(B, T, -1), cn[6].reshape(B, T, -1)]
+    expect = np.concatenate([e.reshape(rows, -1) for e in exp_d], 1)
+    got = proj_d.grad
+    _close_bf16(got[:, :width], expect, "dproj")
+    if W:
+        # parameter gradients: exact sums in fp64 of the same terms
+        dcw = np.zeros((C, W))
+        dcb = np.zeros(C)
+        for i in range(3):
+            c0 = (0, Dk, 2 * Dk)[i]
+            c1 = c0 + (Dk, Dk, Dv)[i]
+            _, dwt, dbt, _ = lo.short_conv_bwd(sec[i], cw.double().numpy()[c0:c1], zs[i],
+                                               cn[i].reshape(B, T, -1),
+                                               None if st is None else _np(st)[:, c0:c1], cu)
+            dcw[c0:c1], dcb[c0:c1] = dwt, dbt
+        scale = float(np.abs(dcw).max())
+        assert_close(cw_d.grad, dcw, "dconv_weight", rtol=1e-3, atol=1e-4 * scale)
+        if cb is not None:
+            assert_close(cb_d.grad, dcb, "dconv_bias", rtol=1e-3, atol=1e-4 * float(np.abs(dcb).max()))
+
+
+@pytest.mark.parametrize("D,rows", [(64, 1000), (128, 777), (256, 300), (128, 20000)])
+def test_norm_gate_matches_oracle(gdn2, D, rows):
+    from importlib import import_module
+    layer = import_module("gateddeltanet-2_b200.layer")
+    gen = torch.Generator().manual_seed(D + rows)
+    x = _bf(torch.randn(rows, D, generator=gen))
+    g = _bf(torch.randn(rows, D, generator=gen) * 2)
+    w = 1 + 0.1 * torch.randn(D, generator=gen)
+    dy = _bf(torch.randn(rows, D, generator=gen))
+    xd, gd, wd = (t.cuda().requires_grad_(True) for t in (x, g, w))
+    y = layer.NormGateFunction.apply(xd, gd, wd, 1e-5)
+    y.backward(dy.cuda())
+    ry, rstd = lo.norm_gate_fwd(_np(x), _np(g), w.double().numpy(), 1e-5)
+    _close_bf16(y, ry, "y")
+    rdx, rdg, rdw = lo.norm_gate_bwd(_np(x), _np(g), w.double().numpy(), rstd, _np(dy))
+    _close_bf16(xd.grad, rdx, "dx")
+    _close_bf16(gd.grad, rdg, "dgate")
+    mass = np.abs(_np(dy) * _np(g) * lo.sigmoid(_np(g)) * _np(x) * rstd).sum(0)
+    err = np.abs(_np(wd.grad) - rdw)
+    assert (err <= 1e-4 + 1e-3 * mass).all(), f"dweight: max err {err.max():.3e}"
+
+
+def _layer_close(name, got, ref, frac=3e-2):
+    a = _np(got) if isinstance(got, torch.Tensor) else np.asarray(got, np.float64)
+    e = np.asarray(ref, np.float64)
+    assert a.shape == e.shape, (name, a.shape, e.shape)
+    assert np.isfinite(a).all(), f"{name}: non-finite"
+    err = np.abs(a - e).max()
+    bound = frac * np.abs(e).max() + 1e-6
+    assert err <= bound, f"{name}: max err {err:.3e} > {bound:.3e} (max |ref| {np.abs(e).max():.3e})"
+
+
+def _run_layer(gdn2, params, x, dout, cfg):
+    from importlib import import_module
+    layer_mod = import_module("gateddeltanet-2_b200.layer")
+    hidden = x.shape[-1]
+    m = layer_mod.GatedDeltaNet2(hidden_size=hidden, head_dim=cfg["head_dim"], num_heads=cfg["num_heads"],
+                                 conv_bias=cfg.get("conv_bias", False),
+                                 allow_neg_eigval=cfg.get("allow_neg_eigval", False), layer_idx=0).cuda()
+    m.load_state_dict({k: torch.as_tensor(v).float() for k, v in params.items()})
+    m.train()
+    xd = torch.as_tensor(x).float().cuda().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = m(xd)[0]
+    out.float().backward(torch.as_tensor(dout).float().cuda())
+    torch.cuda.synchronize()
+    return m, out, xd
+
+
+@pytest.mark.parametrize("name", case_names("layer"))
+def test_layer_matches_reference_layer_golden(gdn2, name):
+    """The CUDA layer (bf16 autocast) against the reference's own layer (fp32)."""
+    meta, t, _ = load_case(name)
+    params = {k[2:]: v for k, v in t.items() if k.startswith("p:")}
+    cfg = dict(num_heads=meta["num_heads"], head_dim=meta["head_dim"], conv_bias=meta["conv_bias"],
+               allow_neg_eigval=meta["allow_neg_eigval"])
+    m, out, xd = _run_layer(gdn2, params, t["x"], t["dout"], cfg)
+    _layer_close("out", out, t["out"])
+    _layer_close("dx", xd.grad, t["dx"])
+    for n, p in m.named_parameters():
+        _layer_close("d" + n, p.grad, t["g:" + n])
+
+
+@pytest.mark.parametrize("hidden,H,Kd,T", [(256, 2, 128, 150), (128, 4, 64, 64)])
+def test_layer_matches_composite_oracle(gdn2, hidden, H, Kd, T):
+    from importlib import import_module
+    layer_mod = import_module("gateddeltanet-2_b200.layer")
+    torch.manual_seed(hidden + T)
+    ref_m = layer_mod.GatedDeltaNet2(hidden_size=hidden, head_dim=Kd, num_heads=H, layer_idx=0)
+    with torch.no_grad():
+        ref_m.o_norm.weight.add_(0.1 * torch.randn_like(ref_m.o_norm.weight))
+        ref_m.g_proj[1].bias.add_(0.1 * torch.randn_like(ref_m.g_proj[1].bias))
+    params = {n: p.detach().numpy().copy() for n, p in ref_m.named_parameters()}
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn(1, T, hidden, generator=gen).numpy()
+    dout = torch.randn(1, T, hidden, generator=gen).numpy()
+    m, out, xd = _run_layer(gdn2, params, x, dout, dict(num_heads=H, head_dim=Kd))
+    rout, G = lo.layer_forward_backward(params, x, dout, dict(num_heads=H, head_dim=Kd, conv_size=4))
+    _layer_close("out", out, rout)
+    _layer_close("dx", xd.grad, G["x"])
+    for n, p in m.named_parameters():
+        _layer_close("d" + n, p.grad, G[n])
+
+
+def test_layer_varlen_mask_matches_separate_sequences(gdn2):
+    """attention_mask unpadding == running each sequence on its own."""
+    from importlib import import_module
+    layer_mod = import_module("gateddeltanet-2_b200.layer")
+    torch.manual_seed(3)
+    m = layer_mod.GatedDeltaNet2(hidden_size=128, head_dim=64, num_heads=2, layer_idx=0).cuda().eval()
+    m.mode = "chunk"
+    lens = [100, 70]
+    x = torch.randn(2, 100, 128, device="cuda")
+    mask = torch.zeros(2, 100, dtype=torch.int64, device="cuda")
+    for i, L in enumerate(lens):
+        mask[i, :L] = 1
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        o = m(x, attention_mask=mask)[0]
+        for i, L in enumerate(lens):
+            oi = m(x[i:i + 1, :L])[0]
+            _layer_close(f"seq{i}", o[i:i + 1, :L], _np(oi), frac=1e-2)
+            assert (o[i, L:] == 0).all()
+
+
+def test_layer_decode_continues_prefill(gdn2):
+    """Prefill with a cache (chunk path), then token-by-token decode (recurrent
+    path, conv and recurrent states from the cache) == one prefill of the whole
+    sequence."""
+    from importlib import import_module
+    layer_mod = import_module("gateddeltanet-2_b200.layer")
+    torch.manual_seed(4)
+    m = layer_mod.GatedDeltaNet2(hidden_size=128, head_dim=64, num_heads=2, layer_idx=0).cuda().eval()
+    T0, steps = 80, 4
+    x = torch.randn(2, T0 + steps, 128, device="cuda")
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        full = m(x)[0]
+        cache = layer_mod.LayerCache()
+        outs = [m(x[:, :T0], past_key_values=cache, use_cache=True)[0]]
+        for s in range(steps):
+            outs.append(m(x[:, T0 + s:T0 + s + 1], past_key_values=cache, use_cache=True)[0])
+    inc = torch.cat(outs, 1)
+    _layer_close("incremental", inc, _np(full), frac=2e-2)
+    assert cache.seen_tokens == T0 + steps
