@@ -19,6 +19,18 @@ line measured with either changed is not a config-2 / config-3 number.
 ``--impl reference`` times the reference's algorithm on the host cores (the
 oracle port: the reference has no CPU implementation of its own and its
 kernels are Triton/sm_120 CUDA); it runs on rank 0 only.
+
+``--impl reference-triton`` times the reference's own Triton op on the GPU
+(the unmodified ``lit_gpt/gdn2_ops`` installed under ``baseline/_ref``) on
+config 2 and config 3, next to this build's op on identical inputs, and
+prints one extra JSON line (``"impl": "reference-triton"``).  Both arms get
+bf16 b, w there: the reference's backward rejects fp32 ``w`` with bf16 ``v``.
+
+``--layer`` measures instead the whole GatedDeltaNet2 token mixer
+(``lit_gpt/gdn2.py``) at the config-4 layer shape (d_model 2048, 16 heads,
+d=128, T=4096, micro-batch 4 per GPU), forward + backward under bf16
+autocast with fp32 parameters (the reference trains ``bf16-mixed``), and
+prints its own JSON line with the layer kernels' rooflines.
 """
 
 from __future__ import annotations
@@ -68,13 +80,15 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--decode-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=B,
                     help="sequences per GPU (config 2 is 4; smaller values are for ncu captures)")
     ap.add_argument("--decode-seqs", type=int, default=DEC_N,
                     help="decode sequences per GPU (config 3 is 256; smaller for ncu captures)")
+    ap.add_argument("--layer", action="store_true",
+                    help="measure the GatedDeltaNet2 layer (config-4 layer shape) instead of the op")
     return ap.parse_args()
 
 
@@ -208,6 +222,224 @@ def cpu_baseline_ours():
 
 
 # ---------------------------------------------------------------------------
+# the reference's own Triton op on the GPU (baseline/_ref)
+# ---------------------------------------------------------------------------
+def load_reference_triton():
+    """``lit_gpt.gdn2_ops`` from ``baseline/_ref`` (unmodified files), imported
+    under a bare parent package: ``lit_gpt/__init__.py`` needs Lightning, which
+    the op does not use."""
+    import types
+    base = os.path.join(ROOT, "baseline", "_ref", "lit_gpt")
+    if not os.path.isdir(os.path.join(base, "gdn2_ops")):
+        raise ImportError("baseline/_ref/lit_gpt/gdn2_ops is not installed")
+    if "lit_gpt" not in sys.modules:
+        pkg = types.ModuleType("lit_gpt")
+        pkg.__path__ = [base]
+        sys.modules["lit_gpt"] = pkg
+    chunk = importlib.import_module("lit_gpt.gdn2_ops.chunk_gdn2")
+    rec = importlib.import_module("lit_gpt.gdn2_ops.fused_recurrent_gdn2")
+    return chunk, rec
+
+
+def run_reference_triton(args, world, rank, local):
+    if rank != 0:
+        return
+    try:
+        ref_chunk, ref_rec = load_reference_triton()
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"impl": "reference-triton", "unavailable": f"{type(e).__name__}: {e}"}), flush=True)
+        return
+    import torch
+    import torch.nn.functional as F
+    gdn2 = importlib.import_module("gateddeltanet-2_b200")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    nb, nd = args.batch, args.decode_seqs
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=gen)
+
+    q = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
+    k = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
+    v = rnd(nb, T, H, V).bfloat16()
+    g = -F.softplus(rnd(nb, T, H, K)) * 0.1
+    b = torch.sigmoid(rnd(nb, T, H, K)).bfloat16()
+    w = torch.sigmoid(rnd(nb, T, H, V)).bfloat16()
+    do = rnd(nb, T, H, V).bfloat16()
+    leaves = [x.requires_grad_(True) for x in (q, k, v, g, b, w)]
+
+    def fwd_bwd(fn):
+        def step():
+            o, _ = fn(*leaves)
+            return torch.autograd.grad(o, leaves, do)
+        return step
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e)
+
+    arms = {"reference": fwd_bwd(ref_chunk.chunk_gdn2), "ours": fwd_bwd(gdn2.chunk_gdn2)}
+    # parity of the two arms on these inputs (max |diff| relative to max |o|)
+    with torch.no_grad():
+        o_r, _ = ref_chunk.chunk_gdn2(q, k, v, g, b, w)
+        o_o, _ = gdn2.chunk_gdn2(q, k, v, g, b, w)
+        rel = float((o_r.float() - o_o.float()).abs().max() / o_r.float().abs().max())
+    res = {}
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local] if vis else local)
+    clocks.start()
+    for name, fn in arms.items():
+        for _ in range(max(3, args.warmup)):
+            fn()
+        ms = timed(fn, args.steps)
+        res[name] = {"ms_per_step": ms / args.steps, "tokens_per_s": nb * T * args.steps / (ms / 1e3)}
+
+    # decode, config 3: in-place state, one token per sequence
+    S_r = rnd(nd, H, K, V) * 0.02
+    S_o = S_r.clone()
+    xs = (F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(), F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
+          rnd(nd, 1, H, V).bfloat16(), -F.softplus(rnd(nd, 1, H, K)) * 0.1,
+          torch.sigmoid(rnd(nd, 1, H, K)), torch.sigmoid(rnd(nd, 1, H, V)))
+    dec = {}
+    for name, fn in (("reference", lambda: ref_rec.fused_recurrent_gdn2_fwd(*xs, initial_state=S_r,
+                                                                           inplace_final_state=True)),
+                     ("ours", lambda: gdn2.fused_recurrent_gdn2_fwd(*xs, initial_state=S_o,
+                                                                   inplace_final_state=True))):
+        for _ in range(10):
+            fn()
+        ms = timed(fn, args.decode_steps)
+        us = 1e3 * ms / args.decode_steps
+        dec[name] = {"us_per_step": us, "state_GBps": decode_bytes_per_step(nd) / (us * 1e-6) / 1e9}
+    clk = clocks.stop()
+    line = {
+        "metric": METRIC, "impl": "reference-triton", "value": res["reference"]["tokens_per_s"],
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": res["reference"]["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config2: GDN2 op fwd+bwd, B={nb} H=16 T=4096 dk=dv=128; "
+                               f"config3 decode N={nd}", "gates": "b, w bf16; log-decay fp32"},
+        "source": "lit_gpt/gdn2_ops from baseline/_ref (the reference's Triton path on sm_100)",
+        "fwd_bwd": res, "speedup_ours_over_reference": res["ours"]["tokens_per_s"] / res["reference"]["tokens_per_s"],
+        "decode": dec, "decode_speedup": dec["reference"]["us_per_step"] / dec["ours"]["us_per_step"],
+        "o_max_rel_diff": rel, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# the GatedDeltaNet2 layer (config-4 layer shape)
+# ---------------------------------------------------------------------------
+D_MODEL = 2048
+
+
+def layer_kernel_bytes_per_token(Dk, Dv, Dfg, H, V):
+    """Algorithmic bytes per token of the layer kernels (each tensor of the
+    kernel's interface read or written once; bf16 activations)."""
+    sec = 2 * (2 * Dk + Dv + Dk + Dv)  # q, k, v, b, w sections
+    fg = 2 * 2 * Dfg
+    return {
+        "layer_prep_fwd_kernel": 2 * (sec + fg),                 # read proj sections, write outputs
+        "layer_prep_bwd_kernel": sec + sec + fg + (sec + fg),    # read proj + cotangents, write dproj
+        "norm_gate_fwd_kernel": 3 * 2 * H * V + 4 * H,           # read x, gate; write y, rstd
+        "norm_gate_bwd_kernel": 5 * 2 * H * V + 4 * H,           # read dy, x, gate, rstd; write dx, dgate
+    }
+
+
+def run_layer(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    layer_mod = importlib.import_module("gateddeltanet-2_b200.layer")
+    from gdn2_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    nb = args.batch
+    torch.manual_seed(1234 + rank)
+    m = layer_mod.GatedDeltaNet2(hidden_size=D_MODEL, head_dim=K, num_heads=H, layer_idx=0).to(dev).train()
+    x = torch.randn(nb, T, D_MODEL, device=dev, dtype=torch.bfloat16).requires_grad_(True)
+    dout = torch.randn(nb, T, D_MODEL, device=dev, dtype=torch.bfloat16)
+    params = list(m.parameters())
+
+    def step():
+        for p in params:
+            p.grad = None
+        x.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = m(x)[0]
+        torch.autograd.backward(out, dout)
+
+    def timed(fn, n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([s.elapsed_time(e)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            dist.barrier()
+        return float(ms.item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local] if vis else local)
+    clocks.start()
+    _lib.profile_enable(True)
+    ms = timed(step, args.steps)
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    clk = clocks.stop()
+    peak, peak_kind = peaks()
+    tok = nb * T
+    bpt = layer_kernel_bytes_per_token(m.key_dim, m.value_dim, m.head_v_dim, H, V)
+    kernels = {}
+    for name, (n, tms) in sorted(prof.items(), key=lambda kv: -kv[1][1]):
+        ent = {"launches": n, "ms_per_step": tms / args.steps, "us_per_launch": 1e3 * tms / max(n, 1)}
+        if name in bpt:
+            achieved = bpt[name] * tok / (tms / max(n, 1) / 1e3) / 1e9
+            ent.update(roofline={"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                 "frac": achieved / peak, "peak_source": peak_kind,
+                                 "algorithmic_bytes_per_launch": bpt[name] * tok})
+        kernels[name] = ent
+    ours_ms = sum(t for _, t in prof.values()) / args.steps
+    step_ms = ms / args.steps
+    if rank == 0:
+        line = {
+            "metric": "GatedDeltaNet2 layer fwd+bwd tokens/s (d2048, H16, d128, T4K)",
+            "value": world * tok * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic, random-init layer",
+            "config": {"workload": f"config-4 layer: GatedDeltaNet2 fwd+bwd, B={nb} T={T} d_model={D_MODEL} "
+                                   "H=16 d=128 conv 4, bf16 autocast, fp32 params",
+                       "global_batch": nb * world, "seq_len": T,
+                       "parallelism": f"data parallel replicas, {world} GPU(s), no gradient all-reduce"},
+            "clocks": clk, "gpu_launches": sum(n for n, _ in prof.values()),
+            "kernels": kernels,
+            "time_split_ms": {"our_kernels": ours_ms, "gemms_and_torch_ops": step_ms - ours_ms},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 def main():
     args = parse()
     nb, nd = args.batch, args.decode_seqs
@@ -218,6 +450,12 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, world)
+        return
+    if args.impl == "reference-triton":
+        run_reference_triton(args, world, rank, local)
+        return
+    if args.layer:
+        run_layer(args, world, rank, local)
         return
 
     cpu_base = None

@@ -64,7 +64,11 @@ const char* gdn2_status_string(int s) {
 
 int gdn2_device_fault_read(int clear, unsigned int* out) {
   if (!out) return GDN2_ERR_NULL_POINTER;
-  return gdn2::tc_fault_read(clear, out);
+  unsigned int a = 0, b = 0;
+  int st = gdn2::tc_fault_read(clear, &a);
+  if (st == 0) st = gdn2::layer_fault_read(clear, &b);
+  *out = a | b;
+  return st;
 }
 
 int gdn2_device_supported(int device) {

@@ -755,12 +755,34 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     }
   }
   __syncthreads();
+  // the chunk's raw gate pre-activations (read by the dg section at the end)
+  // are pulled into L2 now, so that section's loads do not wait on HBM
+  constexpr int kGParts = kBIntraThreads / K, kGRows = kChunk / kGParts;
+  const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
+  if (gate && tid < L) l2_prefetch(a.g + tokK(tid, 0), K * static_cast<int>(sizeof(float)));
   {
     // staged in the phase-3 operand region (dead now), written out below
     __nv_bfloat16 (*sdq)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.QG[0][0]);
     __nv_bfloat16 (*sdk)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.KBG[0][0]);
     TB (*sdb)[S::LB] = reinterpret_cast<TB (*)[S::LB]>(&p3.KN[0][0]);
     static_assert(kChunk * S::LB * sizeof(TB) <= sizeof(p3.KN), "staged db fits the KN operand");
+    // the l2norm row factors of this lane's two rows (loaded once, not per element)
+    float lq[2] = {0.f, 0.f}, lk[2] = {0.f, 0.f}, rsq[2] = {0.f, 0.f}, rsk[2] = {0.f, 0.f};
+    if (l2) {
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const int r = m0 + (lane >> 2) + x * 8;
+        if (r < L) {
+          lq[x] = ws.q_rstd[(t0 + r) * H + h];
+          lk[x] = ws.k_rstd[(t0 + r) * H + h];
+#pragma unroll
+          for (int y = 0; y < 4; ++y) {
+            rsq[x] += sm.rsum[r][y][0];
+            rsk[x] += sm.rsum[r][y][1];
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
@@ -769,13 +791,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         float xq0 = dq[0][j][2 * x], xq1 = dq[0][j][2 * x + 1];
         float xk0 = dk[0][j][2 * x], xk1 = dk[0][j][2 * x + 1];
         if (l2 && r < L) {
-          float sq = 0.f, sk = 0.f;
-#pragma unroll
-          for (int y = 0; y < 4; ++y) {
-            sq += sm.rsum[r][y][0];
-            sk += sm.rsum[r][y][1];
-          }
-          const float rq = ws.q_rstd[(t0 + r) * H + h], rk = ws.k_rstd[(t0 + r) * H + h];
+          const float sq = rsq[x], sk = rsk[x], rq = lq[x], rk = lk[x];
           const float2 q2 = ld2(&sg.Q[r][c]), k2 = ld2(&sg.Kk[r][c]);
           xq0 = (xq0 - sq * q2.x) * rq;
           xq1 = (xq1 - sq * q2.y) * rq;
@@ -803,11 +819,10 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     }
   }
   // dg: reverse cumsum inside the chunk, then the gate VJP.  All threads take
-  // part: channel c = tid % K, row part p = tid / K (kParts parts of the chunk).
-  const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
+  // part: channel c = tid % K, row part p = tid / K (kGParts parts of the chunk).
   const bool lbnd = a.flags & GDN2_LOWER_BOUND;
   {
-    constexpr int kParts = kBIntraThreads / K, kRowsPer = kChunk / kParts;
+    constexpr int kRowsPer = kGRows;
     const int c = tid % K, p = tid / K;
     const int r_lo = p * kRowsPer, r_hi = r_lo + kRowsPer;  // rows [r_lo, r_hi)
     float part = 0.f;
@@ -815,28 +830,42 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     sm.ptot[p][c] = part;
     __syncthreads();
     float acc = 0.f;
-    for (int q2 = p + 1; q2 < kParts; ++q2) acc += sm.ptot[q2][c];
+    for (int q2 = p + 1; q2 < kGParts; ++q2) acc += sm.ptot[q2][c];
     const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
     const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
-    float dA = 0.f, dbias = 0.f;
-    for (int r = r_hi - 1; r >= r_lo; --r) {
-      acc += sm.G[r][c];
-      if (r >= L) continue;
-      const int64_t gi = tokK(r, c);
-      float out = acc;
-      if (gate) {
-        const float x = a.g[gi] + bias;
+    // d(activation)/d(raw) and the A_log factor per row: independent of the
+    // cumsum chain, so computed ahead of it with full ILP
+    float fo[kRowsPer], fa[kRowsPer];
+    if (gate) {
+      float graw[kRowsPer];
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i) graw[i] = (r_lo + i < L) ? a.g[tokK(r_lo + i, c)] : 0.f;
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i) {
+        const float x = graw[i] + bias;
         if (lbnd) {
           const float s2 = sigmoid_f(Aexp * x);
-          out = acc * a.lower_bound * s2 * (1.f - s2) * Aexp;
-          dA += out * x;
+          fo[i] = a.lower_bound * s2 * (1.f - s2) * Aexp;
+          fa[i] = fo[i] * x;
         } else {
-          out = -Aexp * acc * sigmoid_f(x);
-          dA += acc * (-Aexp * softplus_f(x));
+          fo[i] = -Aexp * sigmoid_f(x);
+          fa[i] = -Aexp * softplus_f(x);
         }
+      }
+    }
+    float dA = 0.f, dbias = 0.f;
+#pragma unroll
+    for (int i = kRowsPer - 1; i >= 0; --i) {
+      const int r = r_lo + i;
+      acc += sm.G[r][c];
+      if (r >= L) continue;
+      float out = acc;
+      if (gate) {
+        out = acc * fo[i];
+        dA += acc * fa[i];
         dbias += out;
       }
-      gr.dg[gi] = out;
+      gr.dg[tokK(r, c)] = out;
     }
     if (gate) {
       if (a.dt_bias) atomicAdd(&gr.ddt_bias[h * K + c], dbias);

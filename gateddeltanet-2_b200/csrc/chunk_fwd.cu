@@ -190,14 +190,24 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     const float Aexp = gate ? __expf(a.A_log[h]) : 0.f;
     const float bias = (gate && a.dt_bias) ? a.dt_bias[h * K + c] : 0.f;
     float Gc = 0.f;
-    for (int r = r0; r < r0 + kRows; ++r) {
-      float x = sm.G[r][c];
+    // 8 rows at a time: their gate activations are independent of one another
+    // (ILP for the transcendental chains); only the cumsum is serial
+    for (int rb = r0; rb < r0 + kRows; rb += 8) {
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) xv[u] = sm.G[rb + u][c];
       if (gate) {
-        x += bias;
-        x = lbnd ? a.lower_bound * sigmoid_f(Aexp * x) : -Aexp * softplus_f(x);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float x = xv[u] + bias;
+          xv[u] = lbnd ? a.lower_bound * sigmoid_f(Aexp * x) : -Aexp * softplus_f(x);
+        }
       }
-      if (r < L) Gc += x * kRcpLn2;
-      sm.G[r][c] = Gc;  // padded rows repeat G_last
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (rb + u < L) Gc += xv[u] * kRcpLn2;
+        sm.G[rb + u][c] = Gc;  // padded rows repeat G_last
+      }
     }
     sm.Dblk[part][c] = Gc;
     __syncthreads();

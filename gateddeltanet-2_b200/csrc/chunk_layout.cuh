@@ -98,5 +98,7 @@ int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t
 int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
                        cudaStream_t s);
 int tc_fault_read(int clear, unsigned int* out);
+// fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up
+int layer_fault_read(int clear, unsigned int* out);
 
 }  // namespace gdn2

@@ -84,9 +84,27 @@ GDN2_DEV float exp2_approx(float x) {
   return y;
 }
 
-// softplus with the pass-through above 20 used by the reference's gate
-GDN2_DEV float softplus_f(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
-GDN2_DEV float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
+// softplus with the pass-through above 20 used by the reference's gate:
+// softplus(x) = max(x, 0) + log1p(y), y = e^-|x| in (0, 1].  log1p(y) from the
+// series ln((1+s)/(1-s)) = 2 (s + s^3/3 + s^5/5 + ...) with s = y / (2 + y) <= 1/3
+// (Abramowitz & Stegun 4.1.27); eight terms leave a truncation error below
+// (1/3)^16 / 17 < 2e-9 relative.  Short and branch-free, unlike a general log1p.
+GDN2_DEV float softplus_f(float x) {
+  if (x > 20.f) return x;
+  const float y = __expf(-fabsf(x));
+  const float s = __fdividef(y, 2.f + y), s2 = s * s;
+  float p = 1.f / 15.f;
+  p = fmaf(p, s2, 1.f / 13.f);
+  p = fmaf(p, s2, 1.f / 11.f);
+  p = fmaf(p, s2, 1.f / 9.f);
+  p = fmaf(p, s2, 1.f / 7.f);
+  p = fmaf(p, s2, 1.f / 5.f);
+  p = fmaf(p, s2, 1.f / 3.f);
+  p = fmaf(p, s2, 1.f);
+  return fmaxf(x, 0.f) + 2.f * s * p;
+}
+// fast reciprocal (__fdividef, a few ulp): every use feeds fp32 math or a bf16 result
+GDN2_DEV float sigmoid_f(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // ---------------------------------------------------------------------------
 // bf16 mma.sync m16n8k16 fragments (row.col, fp32 accumulate)

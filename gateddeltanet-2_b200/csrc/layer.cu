@@ -11,19 +11,18 @@
 //   norm_gate_fwd/bwd      FusedRMSNormSwishGate (gdn2.py:462; fla
 //                          fused_norm_gate.py:35-104).
 //
-// Thread layout of the prep kernels: a lane owns NV consecutive channels (a
-// 16-byte vector of a row in the forward, 8-byte in the backward, so a warp
-// touches 512 or 256 contiguous bytes of each row) and a warp walks a segment
-// of kPrepRows rows; the 8 warps of a CTA take 8 consecutive segments of the
-// same 32 x NV channels.  The conv taps of a row are
-// the previous W-1 rows of the same sequence, held in registers while the
-// warp walks forward (forward) or reloaded through L1 (backward, which walks
-// backward so that the W cotangents a row needs are already computed).
+// Thread layout of the prep kernels: a lane owns NV = 4 consecutive channels
+// (an 8-byte vector of a row, so a warp touches 256 contiguous bytes of each
+// row) and a warp walks a segment of kPrepRows rows, kPrepU rows per group of
+// loads; the 8 warps of a CTA take 8 consecutive segments of the same 128
+// channels.  The conv taps of a row are the previous W-1 rows of the same
+// sequence, held in registers while the warp walks forward.
 #include <algorithm>
 
 #include "chunk_layout.cuh"
 #include "common.cuh"
 #include "profile.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 namespace {
@@ -33,18 +32,18 @@ using bf16 = __nv_bfloat16;
 constexpr int kPrepWarps = 8;
 constexpr int kPrepRows = 32;
 constexpr int kPrepRowsPerCta = kPrepWarps * kPrepRows;
+constexpr int kBwdRows = 16;  // backward rows per warp (plus W-1 staged rows after them)
+constexpr int kNV = 4;        // channels per lane
 constexpr int kNormBwdMaxCtas = 1184;  // fixed so the dweight reduction order never depends on the device
 
 struct PrepGeom {
   int64_t C;                 // conv channels 2Dk+Dv (= proj column of b_raw)
-  int64_t Gc, Gs, Gf, G;     // NV-channel groups: conv, sigmoid, copy, total
+  int64_t Gc, Gs, Gf, G;     // 4-channel groups: conv, sigmoid, copy, total
   int64_t off_f;             // proj column of f0 (g0 follows)
-  int64_t grid_y;            // row tiles of kPrepRowsPerCta
+  int64_t grid_y;            // row tiles (rows per CTA: 8 warps x rows per warp)
 };
 
-// NV: channels per lane (8 in the forward, 4 in the backward, whose lanes
-// hold W x NV taps, W x NV conv cotangents and (W+1) x NV partial sums)
-PrepGeom prep_geom(const gdn2_prep_args& a, int NV) {
+PrepGeom prep_geom(const gdn2_prep_args& a, int NV, int rows_per_cta) {
   PrepGeom g;
   g.C = 2 * a.Dk + a.Dv;
   g.Gc = g.C / NV;
@@ -52,7 +51,7 @@ PrepGeom prep_geom(const gdn2_prep_args& a, int NV) {
   g.Gf = a.f0 ? 2 * a.Dfg / NV : 0;
   g.G = g.Gc + g.Gs + g.Gf;
   g.off_f = g.C + a.Dk + a.Dv;
-  g.grid_y = (a.rows + kPrepRowsPerCta - 1) / kPrepRowsPerCta;
+  g.grid_y = (a.rows + rows_per_cta - 1) / rows_per_cta;
   return g;
 }
 
@@ -76,7 +75,7 @@ GDN2_DEV Seq seq_of(const gdn2_prep_args& a, int64_t r) {
   return {lo, a.cu_seqlens[lo], a.cu_seqlens[lo + 1]};
 }
 
-GDN2_DEV float silu(float z) { return z / (1.f + __expf(-z)); }
+GDN2_DEV float silu(float z) { return __fdividef(z, 1.f + __expf(-z)); }
 GDN2_DEV float silu_grad(float z) {
   const float s = sigmoid_f(z);
   return s * (1.f + z * (1.f - s));
@@ -132,223 +131,342 @@ GDN2_DEV OutSlot conv_slot(const gdn2_prep_args& a, int64_t c0) {
   return {reinterpret_cast<bf16*>(a.v), a.Dv, c0 - 2 * a.Dk};
 }
 
-template <int W, int NV>
-__global__ void __launch_bounds__(kPrepWarps * 32) layer_prep_fwd_kernel(gdn2_prep_args a, PrepGeom g) {
+// Fault word of the layer kernels: bit 1 = a bounded wait on a staging
+// barrier gave up (that launch's outputs are invalid).
+__device__ unsigned int g_layer_fault;
+
+// ---------------------------------------------------------------------------
+// bulk staging of a warp's strip: rows [r, r + n) x channels [col0, col0 + 128)
+// ---------------------------------------------------------------------------
+constexpr int kStripCh = 32 * kNV;         // channels of a column tile (a warp's strip)
+constexpr int kStripBytes = kStripCh * 2;  // bf16
+
+// Lane 0 only.  Copies rows [r, r + n) of columns [lo, hi) (channels of the
+// strip starting at col0) from `src` (row stride ld, column c at src + c - base)
+// into buf (kStripCh bf16 per row); returns the bytes it queued.
+GDN2_DEV uint32_t stage_rows(bf16* buf, const bf16* src, int64_t ld, int64_t base, int64_t col0, int64_t lo,
+                             int64_t hi, int64_t r, int n, uint64_t* bar) {
+  if (hi <= lo || !src) return 0;
+  const uint32_t bytes = static_cast<uint32_t>((hi - lo) * 2);
+  const bf16* p = src + r * ld + (lo - base);
+  bf16* d = buf + (lo - col0);
+  for (int i = 0; i < n; ++i) tc::bulk_load(d + i * kStripCh, p + i * ld, bytes, bar);
+  return bytes * n;
+}
+
+// waits for the strip; on a timeout records it, gives the copies one more
+// bounded wait and reports failure (the caller abandons its rows)
+GDN2_DEV bool strip_wait(uint64_t* bar) {
+  if (tc::mbar_wait(bar, 0)) return true;
+  atomicOr(&g_layer_fault, 2u);
+  tc::mbar_wait(bar, 0);
+  return false;
+}
+
+// Forward.  Each warp stages its kPrepRows x 128-channel strip of the
+// projection with bulk copies (all rows in flight at once), then every lane
+// computes its 4 channels row by row from shared memory.
+template <int W>
+__global__ void __launch_bounds__(kPrepWarps * 32, 3) layer_prep_fwd_kernel(gdn2_prep_args a, PrepGeom g) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t grp = static_cast<int64_t>(blockIdx.x) * 32 + lane;
   const int64_t r0 = (static_cast<int64_t>(blockIdx.y) * kPrepWarps + warp) * kPrepRows;
-  if (grp >= g.G || r0 >= a.rows) return;
+  if (r0 >= a.rows) return;  // warps are independent: no CTA barrier below
   const int64_t r1 = min(r0 + kPrepRows, a.rows);
+  const int nrow = static_cast<int>(r1 - r0);
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * kStripCh;
+  const int64_t width = g.G * kNV;  // staged columns: q|k|v|b|w (|f0|g0)
+  bf16* buf = reinterpret_cast<bf16*>(smem_raw) + warp * kPrepRows * kStripCh;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + kPrepWarps * kPrepRows * kStripBytes) + warp;
   const bf16* proj = reinterpret_cast<const bf16*>(a.proj);
-  const int64_t ld = a.proj_stride;
+  if (lane == 0) {
+    tc::mbar_init(bar, 1);
+    tc::mbar_fence_init();
+    const uint32_t bytes = static_cast<uint32_t>((min(col0 + kStripCh, width) - col0) * 2) * nrow;
+    tc::mbar_arrive_expect_tx(bar, bytes);
+    stage_rows(buf, proj, a.proj_stride, 0, col0, col0, min(col0 + kStripCh, width), r0, nrow, bar);
+  }
+  __syncwarp();
+  const int64_t grp = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const bf16* xrow = buf + lane * kNV;  // this lane's 4 channels of staged row 0
 
   if (grp < g.Gc) {  // ---- q, k, v: SiLU(conv) --------------------------------
-    const int64_t c0 = grp * NV;
+    const int64_t c0 = grp * kNV;
     const OutSlot o = conv_slot(a, c0);
-    if constexpr (W == 0) {
-      for (int64_t r = r0; r < r1; ++r) {
-        float x[NV];
-        ldv<NV>(proj + r * ld + c0, x);
+    float wt[W > 0 ? W : 1][kNV], bias[kNV];
+    float win[W > 1 ? W - 1 : 1][kNV];  // win[j]: input of row r - (W-1) + j
+    Seq sq{0, 0, 0};
+    bf16* st_out = reinterpret_cast<bf16*>(a.conv_state_out);
+    if constexpr (W > 0) {  // set up while the strip is in flight
 #pragma unroll
-        for (int i = 0; i < NV; ++i) x[i] = silu(x[i]);
-        stv<NV>(o.p + r * o.ld + o.col, x);
-      }
-    } else {
-      float wt[W][NV], bias[NV];
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
+      for (int i = 0; i < kNV; ++i) {
 #pragma unroll
         for (int j = 0; j < W; ++j) wt[j][i] = a.conv_weight[(c0 + i) * W + j];
         bias[i] = a.conv_bias ? a.conv_bias[c0 + i] : 0.f;
       }
-      float win[W - 1][NV];  // win[j]: input of row r - (W-1) + j
-      Seq sq = seq_of(a, r0);
+      sq = seq_of(a, r0);
 #pragma unroll
-      for (int j = 0; j < W - 1; ++j) conv_tap<W, NV>(a, g, sq, r0 - (W - 1) + j, c0, win[j]);
-      bf16* st_out = reinterpret_cast<bf16*>(a.conv_state_out);
-      for (int64_t r = r0; r < r1; ++r) {
+      for (int j = 0; j < W - 1; ++j) conv_tap<W, kNV>(a, g, sq, r0 - (W - 1) + j, c0, win[j]);
+    }
+    if (!strip_wait(bar)) return;
+    bf16* op = o.p + r0 * o.ld + o.col;
+#pragma unroll 4
+    for (int i = 0; i < nrow; ++i, op += o.ld) {
+      const int64_t r = r0 + i;
+      float x[kNV], y[kNV];
+      ldv<kNV>(xrow + i * kStripCh, x);
+      if constexpr (W == 0) {
+#pragma unroll
+        for (int c = 0; c < kNV; ++c) y[c] = silu(x[c]);
+      } else {
         if (r == sq.e) {  // a new sequence starts: its history is its cache
           sq = seq_of(a, r);
 #pragma unroll
-          for (int j = 0; j < W - 1; ++j) conv_tap<W, NV>(a, g, sq, r - (W - 1) + j, c0, win[j]);
+          for (int j = 0; j < W - 1; ++j) conv_tap<W, kNV>(a, g, sq, r - (W - 1) + j, c0, win[j]);
         }
-        float x[NV], y[NV];
-        ldv<NV>(proj + r * ld + c0, x);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          float z = bias[i] + wt[W - 1][i] * x[i];
+        for (int c = 0; c < kNV; ++c) {
+          float z = bias[c] + wt[W - 1][c] * x[c];
 #pragma unroll
-          for (int j = 0; j < W - 1; ++j) z += wt[j][i] * win[j][i];
-          y[i] = silu(z);
+          for (int j = 0; j < W - 1; ++j) z += wt[j][c] * win[j][c];
+          y[c] = silu(z);
         }
-        stv<NV>(o.p + r * o.ld + o.col, y);
         if (st_out && r == sq.e - 1) {  // the sequence's last W inputs
           bf16* p = st_out + (sq.n * g.C + c0) * W;
 #pragma unroll
-          for (int i = 0; i < NV; ++i) {
+          for (int c = 0; c < kNV; ++c) {
 #pragma unroll
-            for (int j = 0; j < W - 1; ++j) p[i * W + j] = __float2bfloat16_rn(win[j][i]);
-            p[i * W + W - 1] = __float2bfloat16_rn(x[i]);
+            for (int j = 0; j < W - 1; ++j) p[c * W + j] = __float2bfloat16_rn(win[j][c]);
+            p[c * W + W - 1] = __float2bfloat16_rn(x[c]);
           }
         }
 #pragma unroll
-        for (int j = 0; j < W - 2; ++j) {
+        for (int j = 0; j + 1 < W - 1; ++j)
 #pragma unroll
-          for (int i = 0; i < NV; ++i) win[j][i] = win[j + 1][i];
-        }
+          for (int c = 0; c < kNV; ++c) win[j][c] = win[j + 1][c];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) win[W - 2][i] = x[i];
+        for (int c = 0; c < kNV; ++c) win[W - 2][c] = x[c];
       }
+      stv<kNV>(op, y);
     }
   } else if (grp < g.Gc + g.Gs) {  // ---- b, w: sigmoid gates ----------------
-    const int64_t s0 = (grp - g.Gc) * NV;
+    const int64_t s0 = (grp - g.Gc) * kNV;
     const bool is_b = s0 < a.Dk;
     bf16* out = reinterpret_cast<bf16*>(is_b ? a.b : a.w);
     const int64_t old = is_b ? a.Dk : a.Dv, oc = is_b ? s0 : s0 - a.Dk;
     const float sc = is_b ? a.b_scale : 1.f;
-    for (int64_t r = r0; r < r1; ++r) {
-      float x[NV];
-      ldv<NV>(proj + r * ld + g.C + s0, x);
+    if (!strip_wait(bar)) return;
+    bf16* op = out + r0 * old + oc;
+#pragma unroll 4
+    for (int i = 0; i < nrow; ++i, op += old) {
+      float x[kNV];
+      ldv<kNV>(xrow + i * kStripCh, x);
 #pragma unroll
-      for (int i = 0; i < NV; ++i) x[i] = sc * sigmoid_f(x[i]);
-      stv<NV>(out + r * old + oc, x);
+      for (int c = 0; c < kNV; ++c) x[c] = sc * sigmoid_f(x[c]);
+      stv<kNV>(op, x);
     }
-  } else {  // ---- f0, g0: contiguous copies ------------------------------------
-    const int64_t f = (grp - g.Gc - g.Gs) * NV;
+  } else if (grp < g.G) {  // ---- f0, g0: contiguous copies ---------------------
+    const int64_t f = (grp - g.Gc - g.Gs) * kNV;
     const bool is_f = f < a.Dfg;
     bf16* out = reinterpret_cast<bf16*>(is_f ? a.f0 : a.g0);
     const int64_t oc = is_f ? f : f - a.Dfg;
-    for (int64_t r = r0; r < r1; ++r) {
-      float x[NV];
-      ldv<NV>(proj + r * ld + g.off_f + f, x);
-      stv<NV>(out + r * a.Dfg + oc, x);
-    }
+    if (!strip_wait(bar)) return;
+    bf16* op = out + r0 * a.Dfg + oc;
+#pragma unroll 4
+    for (int i = 0; i < nrow; ++i, op += a.Dfg)
+      *reinterpret_cast<uint2*>(op) = *reinterpret_cast<const uint2*>(xrow + i * kStripCh);
+  } else {
+    strip_wait(bar);  // no channels: still let the copies land before the warp exits
   }
 }
 
-// Partial sums per CTA row tile: part[tile][C*W + C] (weights c*W + j, then bias).
-template <int W, int NV>
-__global__ void __launch_bounds__(kPrepWarps * 32)
+// Backward.  Each warp stages the projection and the cotangents of rows
+// [r0, t_end) (its kBwdRows rows and, for the convolution, the W-1 rows after
+// them) with bulk copies; the cotangent strip is assembled from the section
+// tensors it crosses (dq | dk | dv | db | dw | df0 | dg0).  A lane then walks
+// its rows forward: d(pre-activation) dz_t needs the conv inputs of rows
+// t-(W-1)..t (register window, as in the forward) and feeds the input
+// cotangents of rows t-(W-1)..t, whose sums stay pending in registers; row
+// t-(W-1) is complete (and stored) at step t.  Partial sums of the conv
+// parameter gradients per CTA row tile: part[tile][C*W + C] (weights c*W + j,
+// then bias).
+template <int W>
+__global__ void __launch_bounds__(kPrepWarps * 32, 2)
     layer_prep_bwd_kernel(gdn2_prep_args a, gdn2_prep_grads gr, PrepGeom g, float* part) {
-  constexpr int kAcc = (W > 0 ? W + 1 : 1) * NV;  // conv weight + bias sums of a lane's channels
-  __shared__ float red[W > 0 ? kAcc * kPrepWarps * 32 : 1];
+  constexpr int kAcc = (W > 0 ? W + 1 : 1) * kNV;  // conv weight + bias sums of a lane's channels
+  constexpr int kRowsSt = kBwdRows + (W > 0 ? W - 1 : 0);
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t grp = static_cast<int64_t>(blockIdx.x) * 32 + lane;
-  const int64_t r0 = (static_cast<int64_t>(blockIdx.y) * kPrepWarps + warp) * kPrepRows;
-  const bool active = grp < g.G && r0 < a.rows;
-  const int64_t r1 = min(r0 + kPrepRows, a.rows);
+  const int64_t r0 = (static_cast<int64_t>(blockIdx.y) * kPrepWarps + warp) * kBwdRows;
+  const bool rows_ok = r0 < a.rows;
+  const int64_t r1 = min(r0 + kBwdRows, a.rows);
+  const int64_t t_end = W > 0 ? min(r1 + W - 1, a.rows) : r1;
+  const int nst = rows_ok ? static_cast<int>(t_end - r0) : 0;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * kStripCh;
+  const int64_t width = g.G * kNV;
+  const int64_t col1 = min(col0 + kStripCh, width);
+  bf16* bx = reinterpret_cast<bf16*>(smem_raw) + warp * 2 * kRowsSt * kStripCh;
+  bf16* bd = bx + kRowsSt * kStripCh;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + kPrepWarps * 2 * kRowsSt * kStripBytes) + warp;
   const bf16* proj = reinterpret_cast<const bf16*>(a.proj);
   bf16* dproj = reinterpret_cast<bf16*>(gr.dproj);
   const int64_t ld = a.proj_stride;
+  if (rows_ok && lane == 0) {
+    tc::mbar_init(bar, 1);
+    tc::mbar_fence_init();
+    // sections of the strip's columns: [start, end) in proj order, source, row stride
+    const int64_t Dk = a.Dk, Dv = a.Dv, C = g.C, F = g.off_f;
+    const int64_t st[7] = {0, Dk, 2 * Dk, C, C + Dk, F, F + a.Dfg};
+    const int64_t en[7] = {Dk, 2 * Dk, C, C + Dk, C + Dk + Dv, F + a.Dfg, F + 2 * a.Dfg};
+    const bf16* srcs[7] = {reinterpret_cast<const bf16*>(gr.dq), reinterpret_cast<const bf16*>(gr.dk),
+                           reinterpret_cast<const bf16*>(gr.dv), reinterpret_cast<const bf16*>(gr.db),
+                           reinterpret_cast<const bf16*>(gr.dw), reinterpret_cast<const bf16*>(gr.df0),
+                           reinterpret_cast<const bf16*>(gr.dg0)};
+    const int64_t lds[7] = {Dk, Dk, Dv, Dk, Dv, a.Dfg, a.Dfg};
+    uint32_t bytes = static_cast<uint32_t>((col1 - col0) * 2) * nst;
+    for (int k = 0; k < 7; ++k) {
+      const int64_t lo = max(col0, st[k]), hi = min(col1, en[k]);
+      if (hi > lo && srcs[k]) bytes += static_cast<uint32_t>((hi - lo) * 2) * nst;
+    }
+    tc::mbar_arrive_expect_tx(bar, bytes);
+    stage_rows(bx, proj, ld, 0, col0, col0, col1, r0, nst, bar);
+    for (int k = 0; k < 7; ++k)
+      stage_rows(bd, srcs[k], lds[k], st[k], col0, max(col0, st[k]), min(col1, en[k]), r0, nst, bar);
+  }
+  __syncwarp();
+  const int64_t grp = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const bool active = rows_ok && grp < g.G;
+  const bf16* xrow = bx + lane * kNV;
+  const bf16* drow = bd + lane * kNV;
   float acc[kAcc];
 #pragma unroll
   for (int i = 0; i < kAcc; ++i) acc[i] = 0.f;
+  bool staged = true;
+  if (rows_ok) staged = strip_wait(bar);
 
-  if (active && grp < g.Gc) {  // ---- q, k, v --------------------------------------
-    const int64_t c0 = grp * NV;
-    const int64_t sec = c0 < a.Dk ? 0 : (c0 < 2 * a.Dk ? 1 : 2);
-    const bf16* dy_p = reinterpret_cast<const bf16*>(sec == 0 ? gr.dq : (sec == 1 ? gr.dk : gr.dv));
-    const int64_t dld = sec == 2 ? a.Dv : a.Dk, dcol = c0 - sec * a.Dk;
+  if (active && staged && grp < g.Gc) {  // ---- q, k, v ------------------------------
+    const int64_t c0 = grp * kNV;
     if constexpr (W == 0) {
-      for (int64_t r = r0; r < r1; ++r) {
-        float x[NV], dy[NV];
-        ldv<NV>(proj + r * ld + c0, x);
-        ldv<NV>(dy_p + r * dld + dcol, dy);
+      for (int i = 0; i < nst; ++i) {
+        float x[kNV], dy[kNV];
+        ldv<kNV>(xrow + i * kStripCh, x);
+        ldv<kNV>(drow + i * kStripCh, dy);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) dy[i] *= silu_grad(x[i]);
-        stv<NV>(dproj + r * ld + c0, dy);
+        for (int c = 0; c < kNV; ++c) dy[c] *= silu_grad(x[c]);
+        stv<kNV>(dproj + (r0 + i) * ld + c0, dy);
       }
     } else {
-      float wt[W][NV], bias[NV];
+      float wt[W][kNV], bias[kNV];
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
+      for (int c = 0; c < kNV; ++c) {
 #pragma unroll
-        for (int j = 0; j < W; ++j) wt[j][i] = a.conv_weight[(c0 + i) * W + j];
-        bias[i] = a.conv_bias ? a.conv_bias[c0 + i] : 0.f;
+        for (int j = 0; j < W; ++j) wt[j][c] = a.conv_weight[(c0 + c) * W + j];
+        bias[c] = a.conv_bias ? a.conv_bias[c0 + c] : 0.f;
       }
-      float ring[W][NV];  // ring[m]: d(pre-activation) of row t + m (0 past the sequence)
+      float win[W - 1][kNV];   // conv inputs of rows t-(W-1) .. t-1
+      float pend[W - 1][kNV];  // pending input cotangents of rows t-(W-1) .. t-1
+      Seq sq = seq_of(a, r0);
 #pragma unroll
-      for (int m = 0; m < W; ++m)
+      for (int j = 0; j < W - 1; ++j) {
+        conv_tap<W, kNV>(a, g, sq, r0 - (W - 1) + j, c0, win[j]);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) ring[m][i] = 0.f;
-      const int64_t t_hi = min(r1 + W - 1, a.rows) - 1;
-      Seq sq = seq_of(a, t_hi);
-      for (int64_t t = t_hi; t >= r0; --t) {
-        if (t < sq.s) {  // crossed into the previous sequence
+        for (int c = 0; c < kNV; ++c) pend[j][c] = 0.f;
+      }
+      // row `row` is ours to store when it lies in [r0, r1) and in the lane's current sequence
+      auto emit = [&](int64_t row, const float* v) {
+        if (row >= r0 && row < r1 && row >= sq.s) stv<kNV>(dproj + row * ld + c0, v);
+      };
+      bool done = false;
+      for (int i = 0; i < nst; ++i) {
+        const int64_t t = r0 + i;
+        if (t == sq.e) {  // the pending rows of the finished sequence are complete
+#pragma unroll
+          for (int j = 0; j < W - 1; ++j) emit(t - (W - 1) + j, pend[j]);
+          if (t >= r1) {
+            done = true;
+            break;
+          }
           sq = seq_of(a, t);
 #pragma unroll
-          for (int m = 0; m < W; ++m)
+          for (int j = 0; j < W - 1; ++j) {
+            conv_tap<W, kNV>(a, g, sq, t - (W - 1) + j, c0, win[j]);
 #pragma unroll
-            for (int i = 0; i < NV; ++i) ring[m][i] = 0.f;
-        }
-        float xt[W][NV], dy[NV];
-#pragma unroll
-        for (int j = 0; j < W; ++j) conv_tap<W, NV>(a, g, sq, t - (W - 1) + j, c0, xt[j]);
-        ldv<NV>(dy_p + t * dld + dcol, dy);
-#pragma unroll
-        for (int m = W - 1; m > 0; --m)
-#pragma unroll
-          for (int i = 0; i < NV; ++i) ring[m][i] = ring[m - 1][i];
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          float z = bias[i];
-#pragma unroll
-          for (int j = 0; j < W; ++j) z += wt[j][i] * xt[j][i];
-          ring[0][i] = dy[i] * silu_grad(z);
-        }
-        if (t < r1) {
-          float dx[NV];
-#pragma unroll
-          for (int i = 0; i < NV; ++i) {
-            float sacc = 0.f;
-#pragma unroll
-            for (int m = 0; m < W; ++m) sacc += wt[W - 1 - m][i] * ring[m][i];
-            dx[i] = sacc;
-#pragma unroll
-            for (int j = 0; j < W; ++j) acc[j * NV + i] += ring[0][i] * xt[j][i];
-            acc[W * NV + i] += ring[0][i];
+            for (int c = 0; c < kNV; ++c) pend[j][c] = 0.f;
           }
-          stv<NV>(dproj + t * ld + c0, dx);
         }
+        float x[kNV], dy[kNV], dz[kNV], fin[kNV];
+        ldv<kNV>(xrow + i * kStripCh, x);
+        ldv<kNV>(drow + i * kStripCh, dy);
+#pragma unroll
+        for (int c = 0; c < kNV; ++c) {
+          float z = bias[c] + wt[W - 1][c] * x[c];
+#pragma unroll
+          for (int j = 0; j < W - 1; ++j) z += wt[j][c] * win[j][c];
+          dz[c] = dy[c] * silu_grad(z);
+          fin[c] = pend[0][c] + wt[0][c] * dz[c];  // row t-(W-1) is complete
+        }
+        emit(t - (W - 1), fin);
+        if (t < r1) {
+#pragma unroll
+          for (int c = 0; c < kNV; ++c) {
+#pragma unroll
+            for (int j = 0; j < W - 1; ++j) acc[j * kNV + c] += dz[c] * win[j][c];
+            acc[(W - 1) * kNV + c] += dz[c] * x[c];
+            acc[W * kNV + c] += dz[c];
+          }
+        }
+        // shift: pend[j] <- pend[j+1] + wt[j+1] dz ; the newest pending row is t
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j)
+#pragma unroll
+          for (int c = 0; c < kNV; ++c)
+            pend[j][c] = (j + 1 < W - 1 ? pend[j + 1][c] : 0.f) + wt[j + 1][c] * dz[c];
+#pragma unroll
+        for (int j = 0; j + 1 < W - 1; ++j)
+#pragma unroll
+          for (int c = 0; c < kNV; ++c) win[j][c] = win[j + 1][c];
+#pragma unroll
+        for (int c = 0; c < kNV; ++c) win[W - 2][c] = x[c];
+      }
+      // the end of the data completes the rows still pending
+      if (!done && t_end == a.rows) {
+#pragma unroll
+        for (int j = 0; j < W - 1; ++j) emit(t_end - (W - 1) + j, pend[j]);
       }
     }
-  } else if (active && grp < g.Gc + g.Gs) {  // ---- b, w ------------------------------
-    const int64_t s0 = (grp - g.Gc) * NV;
-    const bool is_b = s0 < a.Dk;
-    const bf16* dg = reinterpret_cast<const bf16*>(is_b ? gr.db : gr.dw);
-    const int64_t old = is_b ? a.Dk : a.Dv, oc = is_b ? s0 : s0 - a.Dk;
-    const float sc = is_b ? a.b_scale : 1.f;
-    for (int64_t r = r0; r < r1; ++r) {
-      float x[NV], d[NV];
-      ldv<NV>(proj + r * ld + g.C + s0, x);
-      ldv<NV>(dg + r * old + oc, d);
+  } else if (active && staged && grp < g.Gc + g.Gs) {  // ---- b, w --------------------
+    const int64_t s0 = (grp - g.Gc) * kNV;
+    const float sc = s0 < a.Dk ? a.b_scale : 1.f;
+    bf16* op = dproj + r0 * ld + g.C + s0;
+    const int n = static_cast<int>(r1 - r0);
+#pragma unroll 4
+    for (int i = 0; i < n; ++i, op += ld) {
+      float x[kNV], d[kNV];
+      ldv<kNV>(xrow + i * kStripCh, x);
+      ldv<kNV>(drow + i * kStripCh, d);
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const float sg = sigmoid_f(x[i]);
-        d[i] *= sc * sg * (1.f - sg);
+      for (int c = 0; c < kNV; ++c) {
+        const float sg = sigmoid_f(x[c]);
+        d[c] *= sc * sg * (1.f - sg);
       }
-      stv<NV>(dproj + r * ld + g.C + s0, d);
+      stv<kNV>(op, d);
     }
-  } else if (active) {  // ---- f0, g0 ------------------------------------------------
-    const int64_t f = (grp - g.Gc - g.Gs) * NV;
-    const bool is_f = f < a.Dfg;
-    const bf16* src = reinterpret_cast<const bf16*>(is_f ? gr.df0 : gr.dg0);
-    const int64_t oc = is_f ? f : f - a.Dfg;
+  } else if (active && staged) {  // ---- f0, g0 ----------------------------------------
+    const int64_t f = (grp - g.Gc - g.Gs) * kNV;
+    const bool has = f < a.Dfg ? gr.df0 != nullptr : gr.dg0 != nullptr;
     for (int64_t r = r0; r < r1; ++r) {
-      float x[NV];
-      if (src) {
-        ldv<NV>(src + r * a.Dfg + oc, x);
-      } else {
-#pragma unroll
-        for (int i = 0; i < NV; ++i) x[i] = 0.f;
-      }
-      stv<NV>(dproj + r * ld + g.off_f + f, x);
+      const int i = static_cast<int>(r - r0);
+      *reinterpret_cast<uint2*>(dproj + r * ld + g.off_f + f) =
+          has ? *reinterpret_cast<const uint2*>(drow + i * kStripCh) : make_uint2(0, 0);
     }
   }
 
   if constexpr (W > 0) {
-    // CTA-uniform: only column tiles holding conv channels reduce
+    // CTA-uniform: only column tiles holding conv channels reduce.  The
+    // staging buffers are free once every warp is past its rows.
     if (static_cast<int64_t>(blockIdx.x) * 32 >= g.Gc) return;
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem_raw);
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) red[(k * kPrepWarps + warp) * 32 + lane] = acc[k];
     __syncthreads();
@@ -359,14 +477,21 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
       for (int w = 0; w < kPrepWarps; ++w) sacc += red[(k * kPrepWarps + w) * 32 + ln];
       const int64_t gg = static_cast<int64_t>(blockIdx.x) * 32 + ln;
       if (gg >= g.Gc) continue;
-      const int j = k / NV, i = k % NV;
-      const int64_t c = gg * NV + i;
+      const int j = k / kNV, i = k % kNV;
+      const int64_t c = gg * kNV + i;
       float* pt = part + static_cast<int64_t>(blockIdx.y) * g.C * (W + 1);
       if (j < W) pt[c * W + j] = sacc;
       else pt[g.C * W + c] = sacc;
     }
   }
 }
+
+template <int W>
+constexpr size_t bwd_smem_bytes() {
+  return static_cast<size_t>(kPrepWarps) * 2 * (kBwdRows + (W > 0 ? W - 1 : 0)) * kStripBytes +
+         kPrepWarps * sizeof(uint64_t);
+}
+constexpr size_t kFwdSmemBytes = static_cast<size_t>(kPrepWarps) * kPrepRows * kStripBytes + kPrepWarps * sizeof(uint64_t);
 
 // out_a[i] (i < na) / out_b[i - na] = sum over p of part[p * (na + nb) + i]
 __global__ void reduce_partials_kernel(const float* part, int64_t nparts, int64_t na, int64_t nb, float* out_a,
@@ -506,26 +631,31 @@ int check_prep(const gdn2_prep_args* a, bool need_ptrs = true) {
   return GDN2_OK;
 }
 
-constexpr int kFwdNV = 8, kBwdNV = 4;
-
 template <int W>
 cudaError_t prep_fwd_launch(const gdn2_prep_args& a, cudaStream_t s) {
-  const PrepGeom g = prep_geom(a, kFwdNV);
+  const PrepGeom g = prep_geom(a, kNV, kPrepRowsPerCta);
   const dim3 grid(static_cast<unsigned>((g.G + 31) / 32), static_cast<unsigned>(g.grid_y));
+  cudaError_t e = cudaFuncSetAttribute(layer_prep_fwd_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kFwdSmemBytes));
+  if (e != cudaSuccess) return e;
   ProfScope ps(kKLayerPrepFwd, s);
-  layer_prep_fwd_kernel<W, kFwdNV><<<grid, kPrepWarps * 32, 0, s>>>(a, g);
+  layer_prep_fwd_kernel<W><<<grid, kPrepWarps * 32, kFwdSmemBytes, s>>>(a, g);
   return cudaGetLastError();
 }
 
 template <int W>
 cudaError_t prep_bwd_launch(const gdn2_prep_args& a, const gdn2_prep_grads& gr, float* part, cudaStream_t s) {
-  const PrepGeom g = prep_geom(a, kBwdNV);
+  const PrepGeom g = prep_geom(a, kNV, kPrepWarps * kBwdRows);
   const dim3 grid(static_cast<unsigned>((g.G + 31) / 32), static_cast<unsigned>(g.grid_y));
+  constexpr size_t smem = bwd_smem_bytes<W>();
+  cudaError_t e = cudaFuncSetAttribute(layer_prep_bwd_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
   {
     ProfScope ps(kKLayerPrepBwd, s);
-    layer_prep_bwd_kernel<W, kBwdNV><<<grid, kPrepWarps * 32, 0, s>>>(a, gr, g, part);
+    layer_prep_bwd_kernel<W><<<grid, kPrepWarps * 32, smem, s>>>(a, gr, g, part);
   }
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess || W == 0) return e;
   const int64_t na = g.C * W, nb = g.C;
   reduce_partials_kernel<<<static_cast<unsigned>((na + nb + 255) / 256), 256, 0, s>>>(part, g.grid_y, na, nb,
@@ -534,6 +664,18 @@ cudaError_t prep_bwd_launch(const gdn2_prep_args& a, const gdn2_prep_grads& gr, 
 }
 
 }  // namespace
+
+int layer_fault_read(int clear, unsigned int* out) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_layer_fault, sizeof(v));
+  if (e == cudaSuccess && clear && v) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_layer_fault, &z, sizeof(z));
+  }
+  *out = v;
+  return e == cudaSuccess ? 0 : -static_cast<int>(e);
+}
+
 }  // namespace gdn2
 
 using namespace gdn2;
@@ -557,7 +699,7 @@ int gdn2_layer_prep_fwd(const gdn2_prep_args* a, gdn2_stream_t stream) {
 
 size_t gdn2_layer_prep_bwd_workspace_size(const gdn2_prep_args* a) {
   if (check_prep(a, false) != GDN2_OK || a->conv_size == 0) return 0;
-  const PrepGeom g = prep_geom(*a, kBwdNV);
+  const PrepGeom g = prep_geom(*a, kNV, kPrepWarps * kBwdRows);
   return static_cast<size_t>(g.grid_y * g.C * (a->conv_size + 1)) * sizeof(float);
 }
 

@@ -112,7 +112,7 @@ def test_prep_state_alias_needs_one_token_per_sequence(gdn2):
               conv_weight=p)
     assert lib.gdn2_layer_prep_fwd(a, None) == 7
     assert lib.gdn2_layer_prep_bwd_workspace_size(_prep(gdn2, rows=512, T=512, N=1)) == \
-        2 * (2 * 64 + 64) * 5 * 4  # two row tiles of 256, C conv channels, W taps + bias, fp32
+        4 * (2 * 64 + 64) * 5 * 4  # four row tiles of 128, C conv channels, W taps + bias, fp32
     assert lib.gdn2_layer_prep_bwd_workspace_size(_prep(gdn2, rows=512, T=512, N=1, conv_size=0)) == 0
 
 

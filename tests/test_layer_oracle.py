@@ -75,3 +75,14 @@ def test_layer_composite_matches_reference_layer(name):
         ref = t["g:" + n]
         scale = float(np.abs(ref).max())
         check("d" + n, G[n], ref, rtol=1e-3, atol=1e-4 * scale)
+
+
+@pytest.mark.parametrize("name", case_names("layer"))
+def test_layer_state_dict_matches_reference(gdn2, name):
+    """A reference GatedDeltaNet2 state dict loads into the B200 layer unchanged."""
+    meta, t, _ = load_case(name)
+    ref = {k[2:]: v.shape for k, v in t.items() if k.startswith("p:")}
+    m = gdn2.GatedDeltaNet2(hidden_size=meta["hidden"], head_dim=meta["head_dim"], num_heads=meta["num_heads"],
+                            conv_bias=meta["conv_bias"], allow_neg_eigval=meta["allow_neg_eigval"])
+    ours = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    assert ours == {k: tuple(s) for k, s in ref.items()}
