@@ -26,6 +26,7 @@ HAS_H0 = 1 << 4
 STORE_FINAL = 1 << 5
 SAVE_FOR_BWD = 1 << 6
 BWD_STATE_ONLY = 1 << 7
+G_BF16 = 1 << 8
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64

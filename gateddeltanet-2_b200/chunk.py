@@ -68,7 +68,8 @@ def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, outpu
     dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, b.dtype, w.dtype)
     bw = _bw_dtype(b, w)
     qb, kb, vb = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-    gf = g.to(torch.float32).contiguous()
+    # bf16 g (the layer's gate pre-activation) is read as is; anything else as fp32
+    gf = g.contiguous() if g.dtype == torch.bfloat16 else g.to(torch.float32).contiguous()
     bb, wb = b.to(bw).contiguous(), w.to(bw).contiguous()
     A_log_f = A_log.float().contiguous() if (use_gate_in_kernel and A_log is not None) else None
     dt_f = dt_bias.float().contiguous() if (use_gate_in_kernel and dt_bias is not None) else None
@@ -83,7 +84,7 @@ def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, outpu
         N = B
         NT = B * ((T + CHUNK - 1) // CHUNK)
     geom = (cu, cidx, coff, N, NT)
-    flags = 0
+    flags = _lib.G_BF16 if gf.dtype == torch.bfloat16 else 0
     if use_qk_l2norm_in_kernel:
         flags |= _lib.L2NORM_QK
     if use_gate_in_kernel:

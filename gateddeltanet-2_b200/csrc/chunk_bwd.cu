@@ -759,7 +759,11 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   // are pulled into L2 now, so that section's loads do not wait on HBM
   constexpr int kGParts = kBIntraThreads / K, kGRows = kChunk / kGParts;
   const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
-  if (gate && tid < L) l2_prefetch(a.g + tokK(tid, 0), K * static_cast<int>(sizeof(float)));
+  const bool g16 = a.flags & GDN2_G_BF16;
+  if (gate && tid < L) {
+    if (g16) l2_prefetch(static_cast<const __nv_bfloat16*>(a.g) + tokK(tid, 0), K * 2);
+    else l2_prefetch(static_cast<const float*>(a.g) + tokK(tid, 0), K * 4);
+  }
   {
     // staged in the phase-3 operand region (dead now), written out below
     __nv_bfloat16 (*sdq)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.QG[0][0]);
@@ -838,8 +842,16 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     float fo[kRowsPer], fa[kRowsPer];
     if (gate) {
       float graw[kRowsPer];
+      if (g16) {
+        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(a.g);
 #pragma unroll
-      for (int i = 0; i < kRowsPer; ++i) graw[i] = (r_lo + i < L) ? a.g[tokK(r_lo + i, c)] : 0.f;
+        for (int i = 0; i < kRowsPer; ++i)
+          graw[i] = (r_lo + i < L) ? __bfloat162float(gp[tokK(r_lo + i, c)]) : 0.f;
+      } else {
+        const float* gp = static_cast<const float*>(a.g);
+#pragma unroll
+        for (int i = 0; i < kRowsPer; ++i) graw[i] = (r_lo + i < L) ? gp[tokK(r_lo + i, c)] : 0.f;
+      }
 #pragma unroll
       for (int i = 0; i < kRowsPer; ++i) {
         const float x = graw[i] + bias;
@@ -854,18 +866,29 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       }
     }
     float dA = 0.f, dbias = 0.f;
+    float outv[kRowsPer];  // dg of the rows, stored after the chain
 #pragma unroll
     for (int i = kRowsPer - 1; i >= 0; --i) {
       const int r = r_lo + i;
       acc += sm.G[r][c];
-      if (r >= L) continue;
       float out = acc;
       if (gate) {
-        out = acc * fo[i];
-        dA += acc * fa[i];
+        out = r < L ? acc * fo[i] : 0.f;
+        dA += r < L ? acc * fa[i] : 0.f;
         dbias += out;
       }
-      gr.dg[tokK(r, c)] = out;
+      outv[i] = out;
+    }
+    if (g16) {
+      __nv_bfloat16* dgp = static_cast<__nv_bfloat16*>(gr.dg);
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i)
+        if (r_lo + i < L) dgp[tokK(r_lo + i, c)] = __float2bfloat16_rn(outv[i]);
+    } else {
+      float* dgp = static_cast<float*>(gr.dg);
+#pragma unroll
+      for (int i = 0; i < kRowsPer; ++i)
+        if (r_lo + i < L) dgp[tokK(r_lo + i, c)] = outv[i];
     }
     if (gate) {
       if (a.dt_bias) atomicAdd(&gr.ddt_bias[h * K + c], dbias);

@@ -124,10 +124,22 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     cp_async16(&sm.Q[r][p], qin + gi, ok);
     cp_async16(&sm.Kt[r][p], kin + gi, ok);
   }
-  for (int i = tid; i < kChunk * (K / 4); i += kIntraThreads) {
-    const int r = i / (K / 4), p = (i % (K / 4)) * 4;
-    const bool ok = r < L;
-    cp_async16(&sm.G[r][p], a.g + ((t0 + (ok ? r : 0)) * H + h) * K + p, ok);
+  if (a.flags & GDN2_G_BF16) {  // bf16 g: widened to fp32 on the way into shared memory
+    const __nv_bfloat16* gin = static_cast<const __nv_bfloat16*>(a.g);
+    for (int i = tid; i < kChunk * (K / 8); i += kIntraThreads) {
+      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (r < L) ld8(gin + ((t0 + r) * H + h) * K + p, x);
+      *reinterpret_cast<float4*>(&sm.G[r][p]) = make_float4(x[0], x[1], x[2], x[3]);
+      *reinterpret_cast<float4*>(&sm.G[r][p + 4]) = make_float4(x[4], x[5], x[6], x[7]);
+    }
+  } else {
+    const float* gin = static_cast<const float*>(a.g);
+    for (int i = tid; i < kChunk * (K / 4); i += kIntraThreads) {
+      const int r = i / (K / 4), p = (i % (K / 4)) * 4;
+      const bool ok = r < L;
+      cp_async16(&sm.G[r][p], gin + ((t0 + (ok ? r : 0)) * H + h) * K + p, ok);
+    }
   }
   cp_async_commit();
   cp_async_wait<0>();

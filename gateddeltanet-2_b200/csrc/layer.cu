@@ -493,16 +493,36 @@ constexpr size_t bwd_smem_bytes() {
 }
 constexpr size_t kFwdSmemBytes = static_cast<size_t>(kPrepWarps) * kPrepRows * kStripBytes + kPrepWarps * sizeof(uint64_t);
 
-// out_a[i] (i < na) / out_b[i - na] = sum over p of part[p * (na + nb) + i]
-__global__ void reduce_partials_kernel(const float* part, int64_t nparts, int64_t na, int64_t nb, float* out_a,
-                                       float* out_b) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t n = na + nb;
-  if (i >= n) return;
-  float s = 0.f;
-  for (int64_t p = 0; p < nparts; ++p) s += part[p * n + i];
-  if (i < na) out_a[i] = s;
-  else if (out_b) out_b[i - na] = s;
+// out_a[i] (i < na) / out_b[i - na] = sum over p < nparts of part[p * (na + nb) + i].
+// A CTA owns 32 columns; thread (x, y) sums partials y, y + 32, ... of column
+// x with four running sums (independent loads in flight), then the 32 sums of
+// a column are added in y order: a fixed order, so the result is reproducible.
+constexpr int kRedThreads = 1024;
+__global__ void __launch_bounds__(kRedThreads) reduce_partials_kernel(const float* part, int64_t nparts, int64_t na,
+                                                                      int64_t nb, float* out_a, float* out_b) {
+  __shared__ float red[32][33];
+  const int x = threadIdx.x & 31, y = threadIdx.x >> 5;
+  const int64_t n = na + nb, i = static_cast<int64_t>(blockIdx.x) * 32 + x;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (i < n) {
+    int64_t p = y;
+    for (; p + 96 < nparts; p += 128) {
+      s0 += part[p * n + i];
+      s1 += part[(p + 32) * n + i];
+      s2 += part[(p + 64) * n + i];
+      s3 += part[(p + 96) * n + i];
+    }
+    for (; p < nparts; p += 32) s0 += part[p * n + i];
+  }
+  red[y][x] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (y == 0 && i < n) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) t += red[k][x];
+    if (i < na) out_a[i] = t;
+    else if (out_b) out_b[i - na] = t;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -658,8 +678,8 @@ cudaError_t prep_bwd_launch(const gdn2_prep_args& a, const gdn2_prep_grads& gr, 
   e = cudaGetLastError();
   if (e != cudaSuccess || W == 0) return e;
   const int64_t na = g.C * W, nb = g.C;
-  reduce_partials_kernel<<<static_cast<unsigned>((na + nb + 255) / 256), 256, 0, s>>>(part, g.grid_y, na, nb,
-                                                                                     gr.dconv_weight, gr.dconv_bias);
+  reduce_partials_kernel<<<static_cast<unsigned>((na + nb + 31) / 32), kRedThreads, 0, s>>>(
+      part, g.grid_y, na, nb, gr.dconv_weight, gr.dconv_bias);
   return cudaGetLastError();
 }
 
@@ -798,7 +818,8 @@ int gdn2_norm_gate_bwd(const void* dy, const void* x, const void* gate, const fl
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return -static_cast<int>(e);
-  reduce_partials_kernel<<<static_cast<unsigned>((D + 255) / 256), 256, 0, s>>>(part, nct, D, 0, dweight, nullptr);
+  reduce_partials_kernel<<<static_cast<unsigned>((D + 31) / 32), kRedThreads, 0, s>>>(part, nct, D, 0, dweight,
+                                                                                        nullptr);
   e = cudaGetLastError();
   return e == cudaSuccess ? GDN2_OK : -static_cast<int>(e);
 }

@@ -54,9 +54,11 @@ enum gdn2_flags {
   GDN2_HAS_H0 = 1 << 4,          /* initial_state given */
   GDN2_STORE_FINAL = 1 << 5,     /* write the final state to `ht` */
   GDN2_SAVE_FOR_BWD = 1 << 6,    /* chunk fwd: keep what gdn2_chunk_bwd needs in the workspace */
-  GDN2_BWD_STATE_ONLY = 1 << 7   /* chunk bwd: only the state-cotangent scan (no reference counterpart):
+  GDN2_BWD_STATE_ONLY = 1 << 7,  /* chunk bwd: only the state-cotangent scan (no reference counterpart):
                                     writes dh0 = d(loss)/d(initial state) for the given do and dht;
                                     dq, dk, dv, dg, db, dw may be NULL */
+  GDN2_G_BF16 = 1 << 8           /* chunk fwd/bwd: g (and dg) are bf16 instead of fp32 (the layer's
+                                    gate pre-activation comes out of a bf16 GEMM) */
 };
 
 /* status codes (> 0: invalid argument) */
@@ -99,7 +101,7 @@ typedef struct gdn2_chunk_args {
   const void* q;
   const void* k;
   const void* v;
-  const float* g;        /* log-decay (natural log), or the raw pre-activation */
+  const void* g;         /* log-decay (natural log), or the raw pre-activation: fp32, or bf16 with GDN2_G_BF16 */
   const void* b;
   const void* w;
   const float* A_log;    /* [H]     with GDN2_GATE_IN_KERNEL */
@@ -115,7 +117,7 @@ typedef struct gdn2_chunk_grads {
   void* dq;              /* [B,T,H,K] dtype_qkv */
   void* dk;              /* [B,T,H,K] dtype_qkv */
   void* dv;              /* [B,T,H,V] dtype_qkv */
-  float* dg;             /* [B,T,H,K] fp32 (w.r.t. g as passed: raw when gated in kernel) */
+  void* dg;              /* [B,T,H,K] g's dtype (w.r.t. g as passed: raw when gated in kernel) */
   void* db;              /* [B,T,H,K] dtype_bw */
   void* dw;              /* [B,T,H,V] dtype_bw */
   float* dh0;            /* [N,H,K,V] fp32 when GDN2_HAS_H0, else may be NULL */
