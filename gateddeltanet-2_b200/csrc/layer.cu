@@ -4,7 +4,7 @@
 //   layer_prep_fwd_kernel  merged projection rows q|k|v|b|w|f0|g0 ->
 //                          SiLU(short causal depthwise conv) for q, k, v
 //                          (fla ShortConvolution, gdn2.py:342-367), sigmoid
-//                          gates b, w (gdn2.py:398-399, :412-420), contiguous
+//                          gates b, w (gdn2.py:383-384, :410-412), contiguous
 //                          f0, g0 for the second-stage GEMMs;
 //   layer_prep_bwd_kernel  the reverse pass, with per-CTA conv weight / bias
 //                          partial sums reduced in a fixed order;

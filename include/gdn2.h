@@ -250,7 +250,7 @@ int gdn2_cp_compose_bwd(const float* gathered_maps, const float* gathered_g, int
  *   q, k, v = SiLU(causal depthwise conv1d of q_raw | k_raw | v_raw), the fla
  *             ShortConvolution of gdn2.py:342-367, or SiLU alone when
  *             conv_size == 0 (gdn2.py:369-372);
- *   b = b_scale * sigmoid(b_raw), w = sigmoid(w_raw)  (gdn2.py:398-399, :412-420);
+ *   b = b_scale * sigmoid(b_raw), w = sigmoid(w_raw)  (gdn2.py:383-384, :410-412);
  *   f0, g0 copied out contiguous (inputs of the second-stage GEMMs).
  * Sequences are rows of T tokens, or given by cu_seqlens [N+1] (device int64)
  * over all rows (every sequence non-empty).  conv_state_in / conv_state_out:

@@ -14,7 +14,7 @@ sit around the GDN2 operator:
   holding the last ``W`` inputs, newest at index ``W-1``; the first output of
   a sequence reads cache entries ``1..W-1`` as its history;
 * the sigmoid gates ``b = b_scale * sigmoid(b_raw)``, ``w = sigmoid(w_raw)``
-  (``gdn2.py:398-399``, ``:412-420``);
+  (``gdn2.py:383-384``, ``:410-412``);
 * the gated output norm ``FusedRMSNormSwishGate`` (``gdn2.py:462``;
   ``fla/modules/fused_norm_gate.py:35-104``):
   ``y = x / sqrt(mean(x^2) + eps) * weight * g * sigmoid(g)``.
