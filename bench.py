@@ -26,6 +26,12 @@ config 2 and config 3, next to this build's op on identical inputs, and
 prints one extra JSON line (``"impl": "reference-triton"``).  Both arms get
 bf16 b, w there: the reference's backward rejects fp32 ``w`` with bf16 ``v``.
 
+``--model`` measures the config-4 training step: the 1.33B hybrid LM
+(24 layers alternating GatedDeltaNet2 and 2048-window attention, SwiGLU,
+RMSNorm, vocab 32000) on uniform-random token ids, seq 4096, micro-batch 4
+per GPU, bf16 autocast, fused AdamW step, gradients all-reduced by DDP over
+NCCL when launched with one rank per GPU.
+
 ``--layer`` measures instead the whole GatedDeltaNet2 token mixer
 (``lit_gpt/gdn2.py``) at the config-4 layer shape (d_model 2048, 16 heads,
 d=128, T=4096, micro-batch 4 per GPU), forward + backward under bf16
@@ -89,6 +95,8 @@ def parse():
                     help="decode sequences per GPU (config 3 is 256; smaller for ncu captures)")
     ap.add_argument("--layer", action="store_true",
                     help="measure the GatedDeltaNet2 layer (config-4 layer shape) instead of the op")
+    ap.add_argument("--model", action="store_true",
+                    help="measure the config-4 hybrid LM training step (1.33B, DDP over the ranks)")
     return ap.parse_args()
 
 
@@ -241,13 +249,27 @@ def load_reference_triton():
     return chunk, rec
 
 
+def load_reference_layer():
+    """The reference's ``GatedDeltaNet2`` (``lit_gpt/gdn2.py``, fla's Triton short
+    convolutions and gated norm, the reference's Triton op) from ``baseline/_ref``."""
+    load_reference_triton()
+    return importlib.import_module("lit_gpt.gdn2").GatedDeltaNet2
+
+
 def run_reference_triton(args, world, rank, local):
     if rank != 0:
         return
     try:
         ref_chunk, ref_rec = load_reference_triton()
+        ref_layer = load_reference_layer() if (args.layer or args.model) else None
     except Exception as e:  # noqa: BLE001
         print(json.dumps({"impl": "reference-triton", "unavailable": f"{type(e).__name__}: {e}"}), flush=True)
+        return
+    if args.layer:
+        run_layer(args, 1, 0, local, layer_cls=ref_layer, impl="reference-triton")
+        return
+    if args.model:
+        run_model(args, 1, 0, local, gdn2_cls=ref_layer, impl="reference-triton")
         return
     import torch
     import torch.nn.functional as F
@@ -352,7 +374,7 @@ def layer_kernel_bytes_per_token(Dk, Dv, Dfg, H, V):
     }
 
 
-def run_layer(args, world, rank, local):
+def run_layer(args, world, rank, local, layer_cls=None, impl="ours"):
     import torch
     import torch.distributed as dist
     layer_mod = importlib.import_module("gateddeltanet-2_b200.layer")
@@ -365,7 +387,8 @@ def run_layer(args, world, rank, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     nb = args.batch
     torch.manual_seed(1234 + rank)
-    m = layer_mod.GatedDeltaNet2(hidden_size=D_MODEL, head_dim=K, num_heads=H, layer_idx=0).to(dev).train()
+    m = (layer_cls or layer_mod.GatedDeltaNet2)(hidden_size=D_MODEL, head_dim=K, num_heads=H,
+                                                layer_idx=0).to(dev).train()
     x = torch.randn(nb, T, D_MODEL, device=dev, dtype=torch.bfloat16).requires_grad_(True)
     dout = torch.randn(nb, T, D_MODEL, device=dev, dtype=torch.bfloat16)
     params = list(m.parameters())
@@ -407,7 +430,7 @@ def run_layer(args, world, rank, local):
     clk = clocks.stop()
     peak, peak_kind = peaks()
     tok = nb * T
-    bpt = layer_kernel_bytes_per_token(m.key_dim, m.value_dim, m.head_v_dim, H, V)
+    bpt = layer_kernel_bytes_per_token(m.key_dim, m.value_dim, m.head_v_dim, H, V) if impl == "ours" else {}
     kernels = {}
     for name, (n, tms) in sorted(prof.items(), key=lambda kv: -kv[1][1]):
         ent = {"launches": n, "ms_per_step": tms / args.steps, "us_per_launch": 1e3 * tms / max(n, 1)}
@@ -421,7 +444,7 @@ def run_layer(args, world, rank, local):
     step_ms = ms / args.steps
     if rank == 0:
         line = {
-            "metric": "GatedDeltaNet2 layer fwd+bwd tokens/s (d2048, H16, d128, T4K)",
+            "metric": "GatedDeltaNet2 layer fwd+bwd tokens/s (d2048, H16, d128, T4K)", "impl": impl,
             "value": world * tok * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -433,6 +456,93 @@ def run_layer(args, world, rank, local):
             "clocks": clk, "gpu_launches": sum(n for n, _ in prof.values()),
             "kernels": kernels,
             "time_split_ms": {"our_kernels": ours_ms, "gemms_and_torch_ops": step_ms - ours_ms},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# config 4: the hybrid LM training step
+# ---------------------------------------------------------------------------
+def run_model(args, world, rank, local, gdn2_cls=None, impl="ours"):
+    import torch
+    import torch.distributed as dist
+    importlib.import_module("gateddeltanet-2_b200")
+    from gdn2_b200 import _lib
+    from gdn2_b200 import model as hm
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    nb = args.batch
+    cfg = hm.HybridConfig()
+    torch.manual_seed(1234)  # the same initial weights on every rank
+    net = hm.GPT(cfg, gdn2_cls=gdn2_cls).to(dev)
+    net.init_weights()
+    nparams = hm.num_parameters(net)
+    model = net
+    if world > 1:
+        model = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local], gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(net.parameters(), lr=4e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    tokens = torch.randint(0, cfg.vocab_size, (nb, T + 1), device=dev, generator=gen)
+    idx, tgt = tokens[:, :-1].contiguous(), tokens[:, 1:].contiguous()
+
+    def step():
+        return hm.train_step(model, opt, idx, tgt)
+
+    def timed(fn, n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([s.elapsed_time(e)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            dist.barrier()
+        return float(ms.item())
+
+    for _ in range(max(3, args.warmup)):
+        loss0 = step()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local] if vis else local)
+    clocks.start()
+    _lib.profile_enable(True)
+    ms = timed(step, args.steps)
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    clk = clocks.stop()
+    loss = float(step())
+    step_ms = ms / args.steps
+    ours_ms = sum(t for _, t in prof.values()) / args.steps
+    if rank == 0:
+        line = {
+            "metric": "config-4 hybrid LM training tokens/s (1.33B, GDN2 + 2048-window attention, seq 4096)",
+            "impl": impl,
+            "value": world * nb * T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: uniform-random token ids, random-init weights",
+            "config": {"workload": f"config4: {nparams / 1e9:.2f}B hybrid LM, 24 layers (12 GatedDeltaNet2, 12 "
+                                   "sliding-window attention), d_model 2048, SwiGLU 4608, vocab 32000; fwd + "
+                                   "loss + bwd + fused AdamW step",
+                       "global_batch": nb * world, "seq_len": T, "micro_batch": nb,
+                       "parallelism": f"dp{world} (DistributedDataParallel over NCCL)" if world > 1 else "dp1",
+                       "params": nparams},
+            "clocks": clk, "gpu_launches": sum(n for n, _ in prof.values()),
+            "gdn2_kernels_ms_per_step": ours_ms,
+            "gdn2_kernels": {n: round(1e3 * t / max(c, 1), 1) for n, (c, t) in prof.items()},
+            "loss_after": loss, "loss_first_warmup": float(loss0),
+            "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -456,6 +566,9 @@ def main():
         return
     if args.layer:
         run_layer(args, world, rank, local)
+        return
+    if args.model:
+        run_model(args, world, rank, local)
         return
 
     cpu_base = None
