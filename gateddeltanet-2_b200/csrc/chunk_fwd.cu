@@ -96,7 +96,7 @@ GDN2_DEV float ld_bw(const void* p, int64_t i) {
 
 template <int K, int V, typename TB>
 __global__ void __launch_bounds__(kIntraThreads, 1)
-chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
+chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   using S = IntraSmem<K, V>;
   S& sm = *reinterpret_cast<S*>(smem_raw);
@@ -158,6 +158,27 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws) {
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) breg[u][e] = 0.f;
+    }
+  }
+  // CTAs start in linear order, one per SM: the CTA pf_stride places on takes
+  // this SM's slot next.  Its first operands (q, k, g, b rows) go to L2 now,
+  // behind this CTA's own loads, so its first wait reads L2 instead of HBM.
+  if (pf_stride > 0) {
+    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + pf_stride;
+    if (nxt < (int64_t)gridDim.x * gridDim.y) {
+      const int64_t nh = nxt / gridDim.x;
+      int64_t nn, nci, nbos, nlen;
+      geo.chunk(nxt % gridDim.x, nn, nci);
+      geo.seq(nn, nbos, nlen);
+      const int r = tid & (kChunk - 1), which = tid / kChunk;  // 4 x 64 rows
+      if (r < nlen - nci * kChunk && which < 4) {
+        const int64_t row = ((nbos + nci * kChunk + r) * H + nh) * K;
+        const int gsz = (a.flags & GDN2_G_BF16) ? 2 : 4;
+        if (which == 0) l2_prefetch(qin + row, K * 2);
+        else if (which == 1) l2_prefetch(kin + row, K * 2);
+        else if (which == 2) l2_prefetch(static_cast<const char*>(a.g) + row * gsz, K * gsz);
+        else l2_prefetch(static_cast<const TB*>(a.b) + row, K * (int)sizeof(TB));
+      }
     }
   }
   if (l2) {
@@ -765,7 +786,7 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
     dim3 g1((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKIntra, s);
-    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, sm_count());
     GDN2_LAUNCH_CHECK();
   }
   if (scan_fwd_tc_supported(a)) return scan_fwd_tc_launch(a, ws, s);
@@ -787,7 +808,7 @@ int launch_transition_kv(const gdn2_chunk_args& a, const ChunkWs& ws, float* map
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
     dim3 g1((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKIntra, s);
-    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, sm_count());
     GDN2_LAUNCH_CHECK();
   }
   const size_t sm2 = sizeof(ScanSmem<K>);

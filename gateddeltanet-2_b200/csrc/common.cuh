@@ -59,6 +59,15 @@ GDN2_DEV void l2_prefetch(const void* p, int bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// SMs of the current device (the co-resident CTAs of a one-CTA-per-SM kernel)
+inline int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  return n;
+}
+
 // 2 consecutive elements (8-byte aligned for fp32, 4-byte for bf16)
 GDN2_DEV float2 ld2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 GDN2_DEV float2 ld2(const __nv_bfloat16* p) {
