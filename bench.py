@@ -32,6 +32,12 @@ RMSNorm, vocab 32000) on uniform-random token ids, seq 4096, micro-batch 4
 per GPU, bf16 autocast, fused AdamW step, gradients all-reduced by DDP over
 NCCL when launched with one rank per GPU.
 
+``--cp`` measures config 5: a B=1, H=16, T=131072 prefill (forward) whose T axis
+is split into equal contiguous shards over the ranks (one boundary-map
+all_gather, prefix composition, shard forward from the composed state); the
+whole sequence is fixed, so ``scaling`` is "strong".  Every rank also runs the
+single-GPU forward of the whole sequence and reports how far its shard is from it.
+
 ``--layer`` measures instead the whole GatedDeltaNet2 token mixer
 (``lit_gpt/gdn2.py``) at the config-4 layer shape (d_model 2048, 16 heads,
 d=128, T=4096, micro-batch 4 per GPU), forward + backward under bf16
@@ -95,6 +101,8 @@ def parse():
                     help="decode sequences per GPU (config 3 is 256; smaller for ncu captures)")
     ap.add_argument("--layer", action="store_true",
                     help="measure the GatedDeltaNet2 layer (config-4 layer shape) instead of the op")
+    ap.add_argument("--cp", action="store_true",
+                    help="measure config-5 context-parallel prefill (T=131072 split over the ranks)")
     ap.add_argument("--model", action="store_true",
                     help="measure the config-4 hybrid LM training step (1.33B, DDP over the ranks)")
     return ap.parse_args()
@@ -463,6 +471,91 @@ def run_layer(args, world, rank, local, layer_cls=None, impl="ours"):
 
 
 # ---------------------------------------------------------------------------
+# config 5: context-parallel prefill
+# ---------------------------------------------------------------------------
+CP_T = 131072
+
+
+def run_cp(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    gdn2 = importlib.import_module("gateddeltanet-2_b200")
+    from gdn2_b200 import cp
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    gen = torch.Generator(device=dev).manual_seed(5)  # the same sequence on every rank
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=gen)
+
+    q = F.normalize(rnd(1, CP_T, H, K), dim=-1).bfloat16()
+    k = F.normalize(rnd(1, CP_T, H, K), dim=-1).bfloat16()
+    v = rnd(1, CP_T, H, V).bfloat16()
+    g = -F.softplus(rnd(1, CP_T, H, K)) * 0.1
+    b = torch.sigmoid(rnd(1, CP_T, H, K))
+    w = torch.sigmoid(rnd(1, CP_T, H, V))
+    Ts = CP_T // world
+    shard = [x[:, rank * Ts:(rank + 1) * Ts].contiguous() for x in (q, k, v, g, b, w)]
+
+    def step():
+        with torch.no_grad():
+            return cp.chunk_gdn2_cp(*shard) if world > 1 else gdn2.chunk_gdn2(*shard, output_final_state=True)
+
+    def timed(fn, n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([s.elapsed_time(e)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            dist.barrier()
+        return float(ms.item())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ms = timed(step, args.steps)
+    o, ht = step()
+    with torch.no_grad():
+        o_ref, ht_ref = gdn2.chunk_gdn2(q, k, v, g, b, w, output_final_state=True)
+    err = float((o.float() - o_ref[:, rank * Ts:(rank + 1) * Ts].float()).abs().max())
+    err_t = torch.tensor([err], device=dev)
+    if world > 1:
+        dist.all_reduce(err_t, op=dist.ReduceOp.MAX)
+    st_err = float((ht - ht_ref).abs().max()) if rank == world - 1 else 0.0
+    st_t = torch.tensor([st_err], device=dev)
+    if world > 1:
+        dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        line = {
+            "metric": "config-5 context-parallel prefill tokens/s (B=1, H16, d128, T=131072)",
+            "value": CP_T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "config5: chunk_gdn2 forward of one T=131072 sequence, T split into "
+                                   f"{world} contiguous shard(s), boundary maps all-gathered over NCCL",
+                       "global_batch": 1, "seq_len": CP_T, "heads": H, "head_dim": K,
+                       "parallelism": f"cp{world}"},
+            "o_max_abs_diff_vs_single_gpu": float(err_t.item()),
+            "final_state_max_abs_diff_vs_single_gpu": float(st_t.item()),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # config 4: the hybrid LM training step
 # ---------------------------------------------------------------------------
 def run_model(args, world, rank, local, gdn2_cls=None, impl="ours"):
@@ -569,6 +662,9 @@ def main():
         return
     if args.model:
         run_model(args, world, rank, local)
+        return
+    if args.cp:
+        run_cp(args, world, rank, local)
         return
 
     cpu_base = None
