@@ -27,6 +27,7 @@ STORE_FINAL = 1 << 5
 SAVE_FOR_BWD = 1 << 6
 BWD_STATE_ONLY = 1 << 7
 G_BF16 = 1 << 8
+SKIP_INTRA = 1 << 9
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64

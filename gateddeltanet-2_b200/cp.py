@@ -38,7 +38,12 @@ from .chunk import _chunk_backward, _chunk_forward, chunk_gdn2
 
 
 class CudaBackend:
-    """The B200 kernels behind the C ABI."""
+    """The B200 kernels behind the C ABI.  ``transition`` keeps its workspace,
+    which holds the shard's intra-chunk factors; ``forward`` on the same inputs
+    then runs only the state scan from the composed state (``GDN2_SKIP_INTRA``)."""
+
+    def __init__(self):
+        self._kept = None
 
     def transition(self, q, k, v, g, b, w, *, scale, use_qk_l2norm_in_kernel,
                    use_gate_in_kernel, A_log, dt_bias, lower_bound):
@@ -72,6 +77,8 @@ class CudaBackend:
         with torch.cuda.device(q.device):
             _lib.check(lib.gdn2_cp_transition(args, maps.data_ptr(), ws.data_ptr(), nbytes,
                                               _lib.stream_ptr(q.device)), "gdn2_cp_transition")
+        key = tuple(x.data_ptr() for x in (q, k, v, g, b, w)) + (flags, float(scale))
+        self._kept = (key, args, ws, nbytes, (qb, kb, vb, gf, bb, wb, A_f, dt_f), q.dtype)
         return maps
 
     def compose(self, gathered, rank, state):
@@ -85,6 +92,28 @@ class CudaBackend:
         return state
 
     def forward(self, q, k, v, g, b, w, *, initial_state, **kw):
+        kept, self._kept = self._kept, None
+        flags = (_lib.L2NORM_QK if kw.get("use_qk_l2norm_in_kernel") else 0) | \
+            (_lib.GATE_IN_KERNEL if kw.get("use_gate_in_kernel") else 0) | \
+            (_lib.LOWER_BOUND if (kw.get("use_gate_in_kernel") and kw.get("lower_bound") is not None) else 0)
+        scale = kw.get("scale")
+        key = tuple(x.data_ptr() for x in (q, k, v, g, b, w)) + (flags, float(scale) if scale is not None else None)
+        if kept is not None and kept[0] == key:
+            # the transition's workspace holds this shard's intra-chunk factors: scan only
+            _, targs, ws, nbytes, held, qdtype = kept
+            B, T, H, K = q.shape
+            V = v.shape[-1]
+            o = torch.empty(B, T, H, V, device=q.device, dtype=torch.bfloat16)
+            ht = torch.empty(B, H, K, V, device=q.device, dtype=torch.float32)
+            h0 = initial_state.to(torch.float32).contiguous()
+            args = _lib.ChunkArgs.from_buffer_copy(targs)
+            args.flags = targs.flags | _lib.HAS_H0 | _lib.STORE_FINAL | _lib.SKIP_INTRA
+            args.h0, args.ht, args.o = h0.data_ptr(), ht.data_ptr(), o.data_ptr()
+            with torch.cuda.device(q.device):
+                _lib.check(_lib.load().gdn2_chunk_fwd(args, ws.data_ptr(), nbytes, _lib.stream_ptr(q.device)),
+                           "gdn2_chunk_fwd")
+            del held  # the inputs the factors were computed from stay alive until here
+            return (o if qdtype == torch.bfloat16 else o.to(qdtype)), ht
         with torch.no_grad():
             return chunk_gdn2(q, k, v, g, b, w, initial_state=initial_state,
                               output_final_state=True, **kw)
@@ -93,6 +122,7 @@ class CudaBackend:
     def forward_train(self, q, k, v, g, b, w, *, initial_state, scale, use_qk_l2norm_in_kernel,
                       use_gate_in_kernel, A_log, dt_bias, lower_bound):
         """The shard's forward from ``initial_state``, keeping its backward operands."""
+        self._kept = None  # the backward needs the saving forward's own workspace layout
         o, ht, saved, meta, _, _ = _chunk_forward(
             q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, True, use_qk_l2norm_in_kernel,
             use_gate_in_kernel, None, None, lower_bound, False, True)

@@ -780,7 +780,7 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
 // ---------------------------------------------------------------------------
 template <int K, int V>
 int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
-  if (a.NT > 0) {
+  if (a.NT > 0 && !(a.flags & GDN2_SKIP_INTRA)) {
     const size_t sm1 = sizeof(IntraSmem<K, V>);
     auto k1 = a.dtype_bw == GDN2_BF16 ? chunk_intra_kernel<K, V, __nv_bfloat16> : chunk_intra_kernel<K, V, float>;
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));

@@ -57,8 +57,13 @@ enum gdn2_flags {
   GDN2_BWD_STATE_ONLY = 1 << 7,  /* chunk bwd: only the state-cotangent scan (no reference counterpart):
                                     writes dh0 = d(loss)/d(initial state) for the given do and dht;
                                     dq, dk, dv, dg, db, dw may be NULL */
-  GDN2_G_BF16 = 1 << 8           /* chunk fwd/bwd: g (and dg) are bf16 instead of fp32 (the layer's
+  GDN2_G_BF16 = 1 << 8,          /* chunk fwd/bwd: g (and dg) are bf16 instead of fp32 (the layer's
                                     gate pre-activation comes out of a bf16 GEMM) */
+  GDN2_SKIP_INTRA = 1 << 9       /* chunk fwd (no reference counterpart): the workspace already holds
+                                    the intra-chunk factors of these same inputs and flags, written
+                                    by gdn2_cp_transition or an earlier gdn2_chunk_fwd; only the
+                                    state scan runs (a context-parallel shard's forward from its
+                                    composed entering state reuses its transition's factors) */
 };
 
 /* status codes (> 0: invalid argument) */
