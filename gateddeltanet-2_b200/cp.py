@@ -77,8 +77,10 @@ class CudaBackend:
         with torch.cuda.device(q.device):
             _lib.check(lib.gdn2_cp_transition(args, maps.data_ptr(), ws.data_ptr(), nbytes,
                                               _lib.stream_ptr(q.device)), "gdn2_cp_transition")
-        key = tuple(x.data_ptr() for x in (q, k, v, g, b, w)) + (flags, float(scale))
-        self._kept = (key, args, ws, nbytes, (qb, kb, vb, gf, bb, wb, A_f, dt_f), q.dtype)
+        # the original input tensors are held (not their addresses), so the reuse
+        # below can only ever match these very tensors
+        self._kept = ((q, k, v, g, b, w), (flags, float(scale)), args, ws, nbytes,
+                      (qb, kb, vb, gf, bb, wb, A_f, dt_f), q.dtype)
         return maps
 
     def compose(self, gathered, rank, state):
@@ -97,10 +99,11 @@ class CudaBackend:
             (_lib.GATE_IN_KERNEL if kw.get("use_gate_in_kernel") else 0) | \
             (_lib.LOWER_BOUND if (kw.get("use_gate_in_kernel") and kw.get("lower_bound") is not None) else 0)
         scale = kw.get("scale")
-        key = tuple(x.data_ptr() for x in (q, k, v, g, b, w)) + (flags, float(scale) if scale is not None else None)
-        if kept is not None and kept[0] == key:
+        same = kept is not None and all(x is y for x, y in zip(kept[0], (q, k, v, g, b, w))) and \
+            kept[1] == (flags, float(scale) if scale is not None else None)
+        if same:
             # the transition's workspace holds this shard's intra-chunk factors: scan only
-            _, targs, ws, nbytes, held, qdtype = kept
+            _, _, targs, ws, nbytes, held, qdtype = kept
             B, T, H, K = q.shape
             V = v.shape[-1]
             o = torch.empty(B, T, H, V, device=q.device, dtype=torch.bfloat16)
