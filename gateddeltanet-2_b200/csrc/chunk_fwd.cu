@@ -182,33 +182,42 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride) {
     }
   }
   if (l2) {
-    // warp w owns rows 8w..8w+7; lane owns channels lane, lane+32, ...
-    for (int rr = 0; rr < 8; ++rr) {
-      const int r = warp * 8 + rr;
-      float qv[K / 32], kv[K / 32];
-      float sq = 0.f, sk = 0.f;
+    // warp w owns rows 8w..8w+7.  A lane owns 4 consecutive channels of a row
+    // (kLpr lanes per row, kRpi rows per pass over the warp): pass 1 forms all
+    // 16 squared norms (q and k of 8 rows) and reduces them interleaved, pass 2
+    // scales the rows in place.
+    constexpr int kLpr = K / 4 < 32 ? K / 4 : 32, kRpi = 32 / kLpr, kIt = 8 / kRpi;
+    const int c4 = (lane % kLpr) * 4, rsub = lane / kLpr;
+    float sq[kIt], sk[kIt];
 #pragma unroll
-      for (int j = 0; j < K / 32; ++j) {
-        qv[j] = __bfloat162float(sm.Q[r][lane + 32 * j]);
-        kv[j] = __bfloat162float(sm.Kt[r][lane + 32 * j]);
-        sq += qv[j] * qv[j];
-        sk += kv[j] * kv[j];
+    for (int i = 0; i < kIt; ++i) {
+      const int r = warp * 8 + i * kRpi + rsub;
+      const float2 q01 = ld2(&sm.Q[r][c4]), q23 = ld2(&sm.Q[r][c4 + 2]);
+      const float2 k01 = ld2(&sm.Kt[r][c4]), k23 = ld2(&sm.Kt[r][c4 + 2]);
+      sq[i] = q01.x * q01.x + q01.y * q01.y + q23.x * q23.x + q23.y * q23.y;
+      sk[i] = k01.x * k01.x + k01.y * k01.y + k23.x * k23.x + k23.y * k23.y;
+    }
+#pragma unroll
+    for (int off = kLpr / 2; off > 0; off >>= 1)
+#pragma unroll
+      for (int i = 0; i < kIt; ++i) {
+        sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], off);
+        sk[i] += __shfl_xor_sync(0xffffffffu, sk[i], off);
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, off);
-        sk += __shfl_xor_sync(0xffffffffu, sk, off);
-      }
-      const float rq = rsqrtf(sq + kL2Eps), rk = rsqrtf(sk + kL2Eps);
-      if (save && r < L && lane == 0) {
+    for (int i = 0; i < kIt; ++i) {
+      const int r = warp * 8 + i * kRpi + rsub;
+      const float rq = rsqrtf(sq[i] + kL2Eps), rk = rsqrtf(sk[i] + kL2Eps);
+      if (save && r < L && lane % kLpr == 0) {
         ws.q_rstd[(t0 + r) * H + h] = rq;
         ws.k_rstd[(t0 + r) * H + h] = rk;
       }
-#pragma unroll
-      for (int j = 0; j < K / 32; ++j) {
-        sm.Q[r][lane + 32 * j] = __float2bfloat16_rn(qv[j] * rq);
-        sm.Kt[r][lane + 32 * j] = __float2bfloat16_rn(kv[j] * rk);
-      }
+      const float2 q01 = ld2(&sm.Q[r][c4]), q23 = ld2(&sm.Q[r][c4 + 2]);
+      const float2 k01 = ld2(&sm.Kt[r][c4]), k23 = ld2(&sm.Kt[r][c4 + 2]);
+      *reinterpret_cast<uint2*>(&sm.Q[r][c4]) =
+          make_uint2(pack_bf16(q01.x * rq, q01.y * rq), pack_bf16(q23.x * rq, q23.y * rq));
+      *reinterpret_cast<uint2*>(&sm.Kt[r][c4]) =
+          make_uint2(pack_bf16(k01.x * rk, k01.y * rk), pack_bf16(k23.x * rk, k23.y * rk));
     }
   }
 
