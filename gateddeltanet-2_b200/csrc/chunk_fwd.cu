@@ -125,11 +125,21 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride) {
     cp_async16(&sm.Kt[r][p], kin + gi, ok);
   }
   if (a.flags & GDN2_G_BF16) {  // bf16 g: widened to fp32 on the way into shared memory
+    // every load of the thread is issued before any is used (one HBM round trip, not four)
     const __nv_bfloat16* gin = static_cast<const __nv_bfloat16*>(a.g);
-    for (int i = tid; i < kChunk * (K / 8); i += kIntraThreads) {
-      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
-      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (r < L) ld8(gin + ((t0 + r) * H + h) * K + p, x);
+    constexpr int kGV = kChunk * (K / 8) / kIntraThreads;
+    static_assert(kChunk * (K / 8) % kIntraThreads == 0, "whole 8-channel vectors per thread");
+    uint4 raw[kGV];
+#pragma unroll
+    for (int u = 0; u < kGV; ++u) {
+      const int i = tid + u * kIntraThreads, r = i / (K / 8), p = (i % (K / 8)) * 8;
+      raw[u] = r < L ? *reinterpret_cast<const uint4*>(gin + ((t0 + r) * H + h) * K + p) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kGV; ++u) {
+      const int i = tid + u * kIntraThreads, r = i / (K / 8), p = (i % (K / 8)) * 8;
+      float x[8];
+      ld8(reinterpret_cast<const __nv_bfloat16*>(&raw[u]), x);
       *reinterpret_cast<float4*>(&sm.G[r][p]) = make_float4(x[0], x[1], x[2], x[3]);
       *reinterpret_cast<float4*>(&sm.G[r][p + 4]) = make_float4(x[4], x[5], x[6], x[7]);
     }
