@@ -144,7 +144,10 @@ def layer_forward_backward(params, x, dout, cfg, cu_seqlens=None):
 
     params: name -> array, the reference module's state-dict names.
     x: [B, T, hidden]; dout: cotangent of the output.
-    cfg: dict(num_heads, head_dim, conv_size, use_short_conv, allow_neg_eigval, norm_eps).
+    cfg: dict(num_heads, head_dim, conv_size, use_short_conv, allow_neg_eigval, norm_eps,
+    num_v_heads).  With num_v_heads > num_heads (grouped value heads, ``gdn2.py:395-399``)
+    q, k, g, b and the gate parameters are repeated over each group of value heads
+    before the operator and their gradients summed back over the group.
     Returns (out, grads) with grads[name] for every parameter and grads["x"].
     """
     from . import gdn2_oracle as orc
@@ -154,8 +157,10 @@ def layer_forward_backward(params, x, dout, cfg, cu_seqlens=None):
     dout = np.asarray(dout, np.float64)
     B, T, hid = x.shape
     H, K = cfg["num_heads"], cfg["head_dim"]
+    HV = cfg.get("num_v_heads") or H
+    rep = HV // H
     V = K
-    Dk = Dv = H * K
+    Dk, Dv = H * K, HV * V
     Dfg = V
     W = cfg["conv_size"] if cfg.get("use_short_conv", True) else 0
     bs = 2.0 if cfg.get("allow_neg_eigval", False) else 1.0
@@ -186,9 +191,16 @@ def layer_forward_backward(params, x, dout, cfg, cu_seqlens=None):
     def heads(a, d):
         return a.reshape(B, T, -1, d)
 
-    A_log, dt_bias = P["A_log"], P["dt_bias"]
+    def kheads(a):  # key-side heads, repeated over each group of value heads
+        return np.repeat(heads(a, K), rep, axis=2)
+
+    def ungroup(a):  # gradient of a repeated key-side tensor: sum over the group
+        return a.reshape(B, T, H, rep, K).sum(3).reshape(B, T, Dk)
+
+    A_log = np.repeat(P["A_log"], rep)
+    dt_bias = np.repeat(P["dt_bias"].reshape(H, K), rep, axis=0).reshape(-1)
     # the operator's backward needs d(o); run its forward first for o
-    r = orc.chunk_gdn2(heads(qkv[0], K), heads(qkv[1], K), heads(qkv[2], V), heads(f_pre, K), heads(b, K),
+    r = orc.chunk_gdn2(kheads(qkv[0]), kheads(qkv[1]), heads(qkv[2], V), kheads(f_pre), kheads(b),
                        heads(w, V), use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=A_log,
                        dt_bias=dt_bias, cu_seqlens=cu_seqlens)
     o = r.o
@@ -198,18 +210,21 @@ def layer_forward_backward(params, x, dout, cfg, cu_seqlens=None):
 
     G = {}
     G["o_proj.weight"] = dout.reshape(-1, hid).T @ yflat.reshape(-1, Dv)
-    dy = (dout @ P["o_proj.weight"]).reshape(B, T, H, V)
+    dy = (dout @ P["o_proj.weight"]).reshape(B, T, HV, V)
     do, dgg, G["o_norm.weight"] = norm_gate_bwd(o, heads(g_gate, V), P["o_norm.weight"], rstd, dy)
     dgg = dgg.reshape(B, T, Dv)
     G["g_proj.1.weight"] = dgg.reshape(-1, Dv).T @ sec[6].reshape(-1, Dfg)
     G["g_proj.1.bias"] = dgg.reshape(-1, Dv).sum(0)
     dsec = [None] * 7
     dsec[6] = dgg @ P["g_proj.1.weight"]
-    r = orc.chunk_gdn2(heads(qkv[0], K), heads(qkv[1], K), heads(qkv[2], V), heads(f_pre, K), heads(b, K),
+    r = orc.chunk_gdn2(kheads(qkv[0]), kheads(qkv[1]), heads(qkv[2], V), kheads(f_pre), kheads(b),
                        heads(w, V), use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, A_log=A_log,
                        dt_bias=dt_bias, cu_seqlens=cu_seqlens, do=do)
-    g = r.grads
-    G["A_log"], G["dt_bias"] = g["A_log"], g["dt_bias"]
+    g = dict(r.grads)
+    G["A_log"] = g["A_log"].reshape(H, rep).sum(1)
+    G["dt_bias"] = g["dt_bias"].reshape(H, rep, K).sum(1).reshape(-1)
+    for n in ("q", "k", "g", "b"):
+        g[n] = ungroup(g[n])
     dfp = g["g"].reshape(B, T, Dk)
     G["f_proj.1.weight"] = dfp.reshape(-1, Dk).T @ sec[5].reshape(-1, Dfg)
     dsec[5] = dfp @ P["f_proj.1.weight"]

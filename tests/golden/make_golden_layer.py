@@ -93,7 +93,7 @@ def norm_case(name, seed, R, V, eps):
     _save(name, meta, dict(x=x, gate=gate, weight=w, y=y, dy=dy, dx=x.grad, dgate=gate.grad, dweight=w.grad))
 
 
-def layer_case(name, seed, ref_root, hidden, H, head_dim, T):
+def layer_case(name, seed, ref_root, hidden, H, head_dim, T, num_v_heads=None):
     import shutil
     import sys
 
@@ -105,8 +105,8 @@ def layer_case(name, seed, ref_root, hidden, H, head_dim, T):
     import importlib
     ref = importlib.import_module("refpkg.gdn2")
     torch.manual_seed(seed)
-    layer = ref.GatedDeltaNet2(hidden_size=hidden, head_dim=head_dim, num_heads=H, conv_bias=True,
-                               allow_neg_eigval=True, layer_idx=0)
+    layer = ref.GatedDeltaNet2(hidden_size=hidden, head_dim=head_dim, num_heads=H, num_v_heads=num_v_heads,
+                               conv_bias=True, allow_neg_eigval=True, layer_idx=0)
     with torch.no_grad():  # move the ones / zeros initialisations off their defaults
         layer.o_norm.weight.add_(0.1 * torch.randn_like(layer.o_norm.weight))
         layer.g_proj[1].bias.add_(0.1 * torch.randn_like(layer.g_proj[1].bias))
@@ -122,7 +122,8 @@ def layer_case(name, seed, ref_root, hidden, H, head_dim, T):
     for n, p in layer.named_parameters():
         arrays["p:" + n] = params[n]
         arrays["g:" + n] = p.grad
-    meta = dict(kind="layer", hidden=hidden, num_heads=H, head_dim=head_dim, T=T, conv_size=4,
+    meta = dict(kind="layer", hidden=hidden, num_heads=H, num_v_heads=num_v_heads or H, head_dim=head_dim, T=T,
+                conv_size=4,
                 conv_bias=True, allow_neg_eigval=True, norm_eps=1e-5)
     _save(name, meta, arrays)
 
@@ -140,6 +141,8 @@ def main():
     norm_case("layer_norm_gate_v64", 4, 40, 64, 1e-6)
     if os.path.isdir(args.ref):
         layer_case("layer_full_fp32", 5, args.ref, hidden=64, H=2, head_dim=64, T=100)
+        # grouped value heads: 2 value heads share each key head (the gate runs in torch there)
+        layer_case("layer_gva_fp32", 6, args.ref, hidden=64, H=1, head_dim=64, T=100, num_v_heads=2)
 
 
 if __name__ == "__main__":

@@ -67,7 +67,8 @@ def test_layer_composite_matches_reference_layer(name):
     meta, t, _ = load_case(name)
     params = {k[2:]: v for k, v in t.items() if k.startswith("p:")}
     cfg = dict(num_heads=meta["num_heads"], head_dim=meta["head_dim"], conv_size=meta["conv_size"],
-               allow_neg_eigval=meta["allow_neg_eigval"], norm_eps=meta["norm_eps"])
+               allow_neg_eigval=meta["allow_neg_eigval"], norm_eps=meta["norm_eps"],
+               num_v_heads=meta.get("num_v_heads"))
     out, G = lo.layer_forward_backward(params, t["x"], t["dout"], cfg)
     check("out", out, t["out"], rtol=1e-3, atol=1e-5)
     check("dx", G["x"], t["dx"], rtol=1e-3, atol=1e-5)
@@ -83,6 +84,7 @@ def test_layer_state_dict_matches_reference(gdn2, name):
     meta, t, _ = load_case(name)
     ref = {k[2:]: v.shape for k, v in t.items() if k.startswith("p:")}
     m = gdn2.GatedDeltaNet2(hidden_size=meta["hidden"], head_dim=meta["head_dim"], num_heads=meta["num_heads"],
-                            conv_bias=meta["conv_bias"], allow_neg_eigval=meta["allow_neg_eigval"])
+                            num_v_heads=meta.get("num_v_heads"), conv_bias=meta["conv_bias"],
+                            allow_neg_eigval=meta["allow_neg_eigval"])
     ours = {k: tuple(v.shape) for k, v in m.state_dict().items()}
     assert ours == {k: tuple(s) for k, s in ref.items()}
