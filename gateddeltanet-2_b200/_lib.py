@@ -28,6 +28,8 @@ SAVE_FOR_BWD = 1 << 6
 BWD_STATE_ONLY = 1 << 7
 G_BF16 = 1 << 8
 SKIP_INTRA = 1 << 9
+# enum gdn2_ws_buffer
+WS_CHUNK_STATES = 0
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -98,7 +100,8 @@ _lib = None
 
 # every symbol include/gdn2.h declares
 EXPORTS = (
-    "gdn2_chunk_workspace_size", "gdn2_chunk_bwd_workspace_size", "gdn2_chunk_fwd",
+    "gdn2_chunk_workspace_size", "gdn2_chunk_bwd_workspace_size", "gdn2_chunk_workspace_offset",
+    "gdn2_chunk_fwd", "gdn2_chunk_fwd_static_scratch",
     "gdn2_chunk_bwd", "gdn2_recurrent_fwd", "gdn2_cp_transition", "gdn2_cp_compose",
     "gdn2_cp_compose_bwd",
     "gdn2_status_string", "gdn2_device_supported", "gdn2_abi_version",
@@ -122,6 +125,8 @@ def load() -> ctypes.CDLL:
     lib.gdn2_chunk_workspace_size.restype = ctypes.c_size_t
     lib.gdn2_chunk_bwd_workspace_size.argtypes = [ctypes.POINTER(ChunkArgs)]
     lib.gdn2_chunk_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.gdn2_chunk_workspace_offset.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.c_int]
+    lib.gdn2_chunk_workspace_offset.restype = ctypes.c_size_t
     lib.gdn2_chunk_fwd.argtypes = [ctypes.POINTER(ChunkArgs), _p, ctypes.c_size_t, _p]
     lib.gdn2_chunk_fwd.restype = ctypes.c_int
     lib.gdn2_chunk_bwd.argtypes = [ctypes.POINTER(ChunkArgs), ctypes.POINTER(ChunkGrads), _p,

@@ -206,30 +206,15 @@ class ChunkGDN2Function(torch.autograd.Function):
 def _intermediate_states(ws, args, B, T, H, K, V, NT, transpose):
     """The per-chunk entering states h [B, NT_per_seq, H, K, V] (bf16), as the
     reference returns them with ``return_intermediate_states``."""
-    lib = _lib.load()
-    # the h buffer sits right after v_new in the workspace layout; recover it
-    # through a second layout query with SAVE (offsets are deterministic)
+    off = _lib.load().gdn2_chunk_workspace_offset(args, _lib.WS_CHUNK_STATES)
+    if off == 2 ** 64 - 1:
+        raise RuntimeError("the forward workspace keeps no chunk states for these arguments")
     # the workspace keeps each chunk state transposed, [NT, H, V, K]
-    off = _ws_offset_of_h(args)
     hT = ws[off:off + NT * H * K * V * 2].view(torch.bfloat16).view(NT, H, V, K)
     h = (hT if transpose else hT.transpose(-1, -2)).contiguous()
     if args.cu_seqlens is None:
         return h.view(B, NT // max(B, 1), H, *h.shape[-2:])
     return h.unsqueeze(0)
-
-
-def _ws_offset_of_h(args) -> int:
-    tok = args.B * args.T
-    H, K, V = args.H, args.K, args.V
-
-    def up(x):
-        return (x + 255) & ~255
-
-    off = 0
-    for nbytes in (tok * H * K * 4, tok * H * 64 * 2, tok * H * 64 * 2, tok * H * K * 2,
-                   tok * H * V * 2, tok * H * K * 2, tok * H * K * 2, tok * H * V * 2):
-        off = up(off + nbytes)
-    return off
 
 
 @torch.compiler.disable

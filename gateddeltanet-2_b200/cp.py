@@ -78,8 +78,10 @@ class CudaBackend:
             _lib.check(lib.gdn2_cp_transition(args, maps.data_ptr(), ws.data_ptr(), nbytes,
                                               _lib.stream_ptr(q.device)), "gdn2_cp_transition")
         # the original input tensors are held (not their addresses), so the reuse
-        # below can only ever match these very tensors
-        self._kept = ((q, k, v, g, b, w), (flags, float(scale)), args, ws, nbytes,
+        # below can only ever match these very tensors, unmodified since
+        gated = (A_log, dt_bias) if use_gate_in_kernel else (None, None)
+        self._kept = (_reuse_key((q, k, v, g, b, w) + gated, flags, scale, lower_bound),
+                      (q, k, v, g, b, w) + gated, args, ws, nbytes,
                       (qb, kb, vb, gf, bb, wb, A_f, dt_f), q.dtype)
         return maps
 
@@ -95,12 +97,14 @@ class CudaBackend:
 
     def forward(self, q, k, v, g, b, w, *, initial_state, **kw):
         kept, self._kept = self._kept, None
+        gate = bool(kw.get("use_gate_in_kernel"))
         flags = (_lib.L2NORM_QK if kw.get("use_qk_l2norm_in_kernel") else 0) | \
-            (_lib.GATE_IN_KERNEL if kw.get("use_gate_in_kernel") else 0) | \
-            (_lib.LOWER_BOUND if (kw.get("use_gate_in_kernel") and kw.get("lower_bound") is not None) else 0)
-        scale = kw.get("scale")
-        same = kept is not None and all(x is y for x, y in zip(kept[0], (q, k, v, g, b, w))) and \
-            kept[1] == (flags, float(scale) if scale is not None else None)
+            (_lib.GATE_IN_KERNEL if gate else 0) | \
+            (_lib.LOWER_BOUND if (gate and kw.get("lower_bound") is not None) else 0)
+        A_log, dt_bias = (kw.get("A_log"), kw.get("dt_bias")) if gate else (None, None)
+        same = kept is not None and \
+            kept[0] == _reuse_key((q, k, v, g, b, w, A_log, dt_bias), flags, kw.get("scale"),
+                                  kw.get("lower_bound"))
         if same:
             # the transition's workspace holds this shard's intra-chunk factors: scan only
             _, _, targs, ws, nbytes, held, qdtype = kept
@@ -148,6 +152,16 @@ class CudaBackend:
     def backward(self, data, do, dS_out):
         """(dq, dk, dv, dg, db, dw, dA_log, ddt_bias, d entering state) of the shard."""
         return _chunk_backward(data[0], data[1], do, dS_out)
+
+
+def _reuse_key(tensors, flags, scale, lower_bound):
+    """What decides whether a shard's forward may reuse its transition's
+    intra-chunk factors: the identity and in-place version of every tensor the
+    factors depend on (q, k, v, g, b, w and, with the gate in the kernel,
+    A_log and dt_bias), the flags, the scale and the lower bound."""
+    ident = tuple((id(t), t._version) if t is not None else None for t in tensors)
+    lb = float(lower_bound) if (flags & _lib.LOWER_BOUND) and lower_bound is not None else None
+    return ident, flags, float(scale) if scale is not None else None, lb
 
 
 def _gather(x, group, world):

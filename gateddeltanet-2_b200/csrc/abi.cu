@@ -83,6 +83,19 @@ size_t gdn2_chunk_workspace_size(const gdn2_chunk_args* a) {
   return chunk_ws_layout(*a, nullptr, nullptr);
 }
 
+size_t gdn2_chunk_workspace_offset(const gdn2_chunk_args* a, int which) {
+  if (check_chunk(a, false) != GDN2_OK) return ~size_t(0);
+  // carve a fake base: offsets are the pointers' distance from it
+  char* const base = reinterpret_cast<char*>(size_t(1) << 40);
+  ChunkWs ws;
+  chunk_ws_layout(*a, base, &ws);
+  switch (which) {
+    case GDN2_WS_CHUNK_STATES:
+      return ws.h ? (size_t)(reinterpret_cast<char*>(ws.h) - base) : ~size_t(0);
+    default: return ~size_t(0);
+  }
+}
+
 size_t gdn2_chunk_bwd_workspace_size(const gdn2_chunk_args* a) {
   if (check_chunk(a, false) != GDN2_OK) return 0;
   return bwd_ws_layout(*a, nullptr, nullptr);

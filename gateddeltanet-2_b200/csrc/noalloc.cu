@@ -20,7 +20,10 @@
 //   * host code cannot use the array's name as a device address.  The first
 //     call on each device (with that device current) asks the runtime for the
 //     address with cudaGetSymbolAddress and caches it; make that first call
-//     before any stream capture.
+//     before any stream capture.  The cache is keyed by device ordinal, so it
+//     holds for the device's primary context (the one the runtime API uses):
+//     a caller that makes another driver context current, or that resets the
+//     device (cudaDeviceReset), must restart the process before calling again.
 #include <mutex>
 
 #include "chunk_layout.cuh"
@@ -58,6 +61,9 @@ extern "C" int gdn2_chunk_fwd_static_scratch(const gdn2_chunk_args* a, gdn2_stre
   if (!a) return GDN2_ERR_NULL_POINTER;
   // the backward reads a context that must outlive this call: not here
   if (a->flags & GDN2_SAVE_FOR_BWD) return GDN2_ERR_FLAGS;
+  // skipping the intra kernel would scan whatever factors the previous call
+  // (possibly another problem, or another caller) left in the shared array
+  if (a->flags & GDN2_SKIP_INTRA) return GDN2_ERR_FLAGS;
   const size_t need = gdn2_chunk_workspace_size(a);
   if (need == 0) return gdn2_chunk_fwd(a, nullptr, 0, stream);  // empty problem, or the argument error
   if (need > kStaticScratchBytes) return GDN2_ERR_SCRATCH_LIMIT;

@@ -137,6 +137,17 @@ size_t gdn2_chunk_workspace_size(const gdn2_chunk_args* a);
 /* Bytes of additional scratch gdn2_chunk_bwd needs (state cotangents, dv). */
 size_t gdn2_chunk_bwd_workspace_size(const gdn2_chunk_args* a);
 
+/* Buffers of the forward workspace a caller may read after gdn2_chunk_fwd. */
+enum gdn2_ws_buffer {
+  GDN2_WS_CHUNK_STATES = 0 /* per-chunk entering states h, bf16, transposed [NT, H, V, K];
+                              present with GDN2_SAVE_FOR_BWD */
+};
+/* Byte offset of buffer `which` inside the workspace gdn2_chunk_fwd fills for
+ * these arguments, or (size_t)-1 when these arguments keep no such buffer
+ * (no counterpart in the reference, whose Python op returns h as a tensor
+ * with return_intermediate_states, chunk_gdn2.py:1495-1511). */
+size_t gdn2_chunk_workspace_offset(const gdn2_chunk_args* a, int which);
+
 int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* workspace, size_t workspace_bytes,
                    gdn2_stream_t stream);
 /* `workspace` must hold what gdn2_chunk_fwd wrote with GDN2_SAVE_FOR_BWD for
@@ -154,7 +165,9 @@ int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr,
  * entry points, and its Python ops allocate through torch.
  *
  * Same arguments and results as gdn2_chunk_fwd without GDN2_SAVE_FOR_BWD
- * (that flag is rejected: a backward needs a context that outlives the call).
+ * (that flag is rejected: a backward needs a context that outlives the call)
+ * and without GDN2_SKIP_INTRA (also rejected: the shared array may hold
+ * another problem's factors).
  * The scratch is one 32 MiB device array inside the library, present on every
  * GPU that loads it until the process exits; problems whose
  * gdn2_chunk_workspace_size exceeds 32 MiB return GDN2_ERR_SCRATCH_LIMIT (about
@@ -163,6 +176,9 @@ int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr,
  * serialise them.  Nothing in it needs clearing between calls.  The first call
  * on each device resolves the array's device address (cudaGetSymbolAddress,
  * with that device current); make that first call before any stream capture.
+ * The address is cached per device ordinal, i.e. for the device's primary
+ * context: after cudaDeviceReset, or with another driver context current,
+ * restart the process before calling again.
  * Nothing is allocated, by this call or by anything it calls.
  */
 int gdn2_chunk_fwd_static_scratch(const gdn2_chunk_args* a, gdn2_stream_t stream);

@@ -243,9 +243,12 @@ RECURRENT_CASES = {
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("GDN2_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("GDN2_REFERENCE_ROOT"),
+                    help="checkout of the reference repository (or set GDN2_REFERENCE_ROOT)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or GDN2_REFERENCE_ROOT")
     import torch
     torch.set_num_threads(os.cpu_count() or 1)
     chunk_mod, rec_mod, tmp = _install_shims(args.ref)

@@ -131,7 +131,9 @@ def layer_case(name, seed, ref_root, hidden, H, head_dim, T, num_v_heads=None):
 def main():
     import argparse
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("GDN2_REFERENCE_ROOT"),
+                    help="checkout of the reference repository (or set GDN2_REFERENCE_ROOT); "
+                         "without it only the fla conv / norm cases are made")
     args = ap.parse_args()
     _shims()
     conv_case("layer_conv_varlen_h0", 0, 1, 100, 64, 4, cu_seqlens=[0, 2, 7, 39, 100], h0=True)
@@ -139,7 +141,7 @@ def main():
     conv_case("layer_conv_k3", 2, 1, 40, 16, 3, cu_seqlens=[0, 17, 40], h0=True)
     norm_case("layer_norm_gate_v128", 3, 96, 128, 1e-5)
     norm_case("layer_norm_gate_v64", 4, 40, 64, 1e-6)
-    if os.path.isdir(args.ref):
+    if args.ref and os.path.isdir(args.ref):
         layer_case("layer_full_fp32", 5, args.ref, hidden=64, H=2, head_dim=64, T=100)
         # grouped value heads: 2 value heads share each key head (the gate runs in torch there)
         layer_case("layer_gva_fp32", 6, args.ref, hidden=64, H=1, head_dim=64, T=100, num_v_heads=2)

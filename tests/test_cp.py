@@ -317,3 +317,24 @@ def test_cp_nccl_two_gpus():
     r = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "CP_OK" in r.stdout
+
+
+def test_factor_reuse_key_tracks_every_dependency(gdn2):
+    """The CUDA backend reuses a transition's intra-chunk factors only for the
+    very tensors it saw, unmodified, with the same gate parameters and flags."""
+    key = gdn2.cp._reuse_key
+    L = gdn2._lib
+    t = [torch.zeros(2) for _ in range(8)]
+    flags = L.GATE_IN_KERNEL | L.LOWER_BOUND
+    base = key(t, flags, 0.1, -1.0)
+    assert key(t, flags, 0.1, -1.0) == base
+    assert key(t, flags, 0.1, -2.0) != base           # another lower bound
+    assert key(t, flags, 0.2, -1.0) != base           # another scale
+    assert key(t, L.GATE_IN_KERNEL, 0.1, -1.0) != base
+    other = list(t)
+    other[6] = torch.zeros(2)                          # another A_log tensor
+    assert key(other, flags, 0.1, -1.0) != base
+    t[7].add_(1.0)                                     # dt_bias edited in place
+    assert key(t, flags, 0.1, -1.0) != base
+    # without LOWER_BOUND the bound's value is irrelevant
+    assert key(t, 0, 0.1, -1.0) == key(t, 0, 0.1, -3.0)

@@ -105,3 +105,7 @@ def test_static_scratch_rejects_oversized_and_backward_contexts(gdn2):
                         q=p, k=p, v=p, g=p, b=p, w=p, o=p)
     assert fwd_static(ctypes.addressof(small), None) == 7
     assert np.isfinite(lib.gdn2_chunk_workspace_size(small))
+    # reusing intra-chunk factors is refused: the shared array may hold another problem's
+    skip = L.ChunkArgs.from_buffer_copy(small)
+    skip.flags = L.SKIP_INTRA
+    assert fwd_static(ctypes.addressof(skip), None) == 7
