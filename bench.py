@@ -6,11 +6,29 @@ Metric: "GDN2 op fwd+bwd tokens/s (H16,d128,T4K) & decode-step state HBM GB/s".
 One step = forward + backward of ``chunk_gdn2`` on config 2 (B=4, H=16,
 T=4096, d_k=d_v=128, chunk 64; q,k,v bf16 with q,k L2-normalised, b,w =
 sigmoid(N(0,1)) fp32, log-decay = -softplus(N(0,1))*0.1 fp32), synthetic
-data.  Every rank processes its own independent batch of config-2 sequences
-(the (batch x head) units shard over GPUs with no communication), so the
-per-GPU work is fixed and ``scaling`` is "weak".  The decode step (config 3:
-N=256 sequences, H=16, 128x128 fp32 state, updated in place) is measured in
-the same run and reported under ``decode``.
+data.  The 64 (sequence, head) pairs of that fixed workload are split over
+the ranks (rank r takes heads [r 16/N, (r+1) 16/N) of all four sequences; no
+communication), so ``value`` is the whole job's tokens/s with strong
+scaling: 64, 32, 16, 8 pairs per GPU at N = 1, 2, 4, 8.  With few pairs per
+GPU the library cuts the state scans into segments to keep the SMs busy.
+
+The same JSON line carries, as extra keys:
+  ``weak``      config 2 with B=4 x 16 heads on every rank (N > 1);
+  ``e2e``       the strong-split step through ``chunk_gdn2`` with every step's
+                inputs copied from pinned host memory (each rank its own heads);
+  ``decode``    config 3: 256 sequences x 16 heads, fp32 128x128 states updated in
+                place, split over the ranks by sequence (strong), 1024 steps;
+  ``cp``        config 5: one T=131072 sequence, forward, T split over the ranks
+                (one all_gather of boundary maps over NCCL; N=1 is the
+                single-GPU forward), each shard checked against the single-GPU result;
+  ``model``     config 4: the 1.33B hybrid LM training step, micro-batch 4 per GPU,
+                DistributedDataParallel over NCCL for N > 1;
+  ``reference_triton`` (N=1) the reference's own Triton op on the same GPU and inputs,
+                configs 2 and 3 (``lit_gpt/gdn2_ops`` from ``baseline/_ref``);
+  ``cpu_baseline`` / ``cpu_baselines`` (N=1) the host cores: the fp64 oracle port
+                of the algorithm, the naive fp32 torch recurrence with autograd
+                (config 1, and config 2 per token-head) and the naive torch decode
+                step (config 3).
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
 (multi-GPU through ``torch.distributed.run``; one rank per GPU).
@@ -19,30 +37,11 @@ line measured with either changed is not a config-2 / config-3 number.
 ``--impl reference`` times the reference's algorithm on the host cores (the
 oracle port: the reference has no CPU implementation of its own and its
 kernels are Triton/sm_120 CUDA); it runs on rank 0 only.
-
-``--impl reference-triton`` times the reference's own Triton op on the GPU
-(the unmodified ``lit_gpt/gdn2_ops`` installed under ``baseline/_ref``) on
-config 2 and config 3, next to this build's op on identical inputs, and
-prints one extra JSON line (``"impl": "reference-triton"``).  Both arms get
-bf16 b, w there: the reference's backward rejects fp32 ``w`` with bf16 ``v``.
-
-``--model`` measures the config-4 training step: the 1.33B hybrid LM
-(24 layers alternating GatedDeltaNet2 and 2048-window attention, SwiGLU,
-RMSNorm, vocab 32000) on uniform-random token ids, seq 4096, micro-batch 4
-per GPU, bf16 autocast, fused AdamW step, gradients all-reduced by DDP over
-NCCL when launched with one rank per GPU.
-
-``--cp`` measures config 5: a B=1, H=16, T=131072 prefill (forward) whose T axis
-is split into equal contiguous shards over the ranks (one boundary-map
-all_gather, prefix composition, shard forward from the composed state); the
-whole sequence is fixed, so ``scaling`` is "strong".  Every rank also runs the
-single-GPU forward of the whole sequence and reports how far its shard is from it.
-
-``--layer`` measures instead the whole GatedDeltaNet2 token mixer
-(``lit_gpt/gdn2.py``) at the config-4 layer shape (d_model 2048, 16 heads,
-d=128, T=4096, micro-batch 4 per GPU), forward + backward under bf16
-autocast with fp32 parameters (the reference trains ``bf16-mixed``), and
-prints its own JSON line with the layer kernels' rooflines.
+``--impl reference-triton`` prints the reference-Triton comparison alone
+(bf16 b, w in both arms: the reference's backward rejects fp32 ``w`` with
+bf16 ``v``); with ``--layer`` / ``--model`` the reference's whole layer.
+``--cp``, ``--model`` and ``--layer`` print the config-5, config-4 and
+GatedDeltaNet2-layer (config-4 layer shape) measurements as lines of their own.
 """
 
 from __future__ import annotations
@@ -95,6 +94,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-triton"])
     ap.add_argument("--decode-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip the reference Triton op in the default N=1 line (its autotuning takes minutes)")
     ap.add_argument("--batch", type=int, default=B,
                     help="sequences per GPU (config 2 is 4; smaller values are for ncu captures)")
     ap.add_argument("--decode-seqs", type=int, default=DEC_N,
@@ -190,33 +191,142 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm: the reference's algorithm on the host cores
+# ranks and device timing
+# ---------------------------------------------------------------------------
+class Ranks:
+    """World, rank and device of this process, with max-over-ranks timing."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
+        self.dist = None
+
+    def init_gpu(self, timeout_s=180):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = dist
+        if self.world > 1 and not dist.is_initialized():
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        import torch
+        if self.world == 1:
+            return float(x)
+        t = torch.tensor([float(x)], device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(self, fn, n) -> float:
+        """ms for n calls of fn on this rank's current stream, max over ranks;
+        a barrier and a device synchronize on both sides."""
+        import torch
+        self.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        ms = self.max(s.elapsed_time(e))
+        self.barrier()
+        return ms
+
+    def clocks(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return ClockSampler(vis.split(",")[self.local] if vis else self.local)
+
+    def close(self):
+        if self.world > 1 and self.dist is not None and self.dist.is_initialized():
+            self.dist.destroy_process_group()
+
+    def solo(self):
+        """This process alone (rank 0 of an arm that runs without the others):
+        no process group, no collectives."""
+        r = Ranks()
+        r.world, r.rank, r.local = 1, 0, self.local
+        return r
+
+
+def config2_inputs(dev, nb, heads, seed, bf16_gates=False):
+    """Config-2 inputs of nb sequences x `heads` heads, generated on the device."""
+    import torch
+    import torch.nn.functional as F
+    gen = torch.Generator(device=dev).manual_seed(seed)
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=gen)
+
+    gd = torch.bfloat16 if bf16_gates else torch.float32
+    q = F.normalize(rnd(nb, T, heads, K), dim=-1).bfloat16()
+    k = F.normalize(rnd(nb, T, heads, K), dim=-1).bfloat16()
+    v = rnd(nb, T, heads, V).bfloat16()
+    g = -F.softplus(rnd(nb, T, heads, K)) * 0.1
+    b = torch.sigmoid(rnd(nb, T, heads, K)).to(gd)
+    w = torch.sigmoid(rnd(nb, T, heads, V)).to(gd)
+    do = rnd(nb, T, heads, V).bfloat16()
+    return q, k, v, g, b, w, do
+
+
+def decode_inputs(dev, nd, seed):
+    import torch
+    import torch.nn.functional as F
+    gen = torch.Generator(device=dev).manual_seed(seed)
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=gen)
+
+    S = rnd(nd, H, K, V) * 0.02
+    ring = [(F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(), F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
+             rnd(nd, 1, H, V).bfloat16(), -F.softplus(rnd(nd, 1, H, K)) * 0.1,
+             torch.sigmoid(rnd(nd, 1, H, K)), torch.sigmoid(rnd(nd, 1, H, V))) for _ in range(4)]
+    return S, ring
+
+
+# ---------------------------------------------------------------------------
+# host-core baselines
 # ---------------------------------------------------------------------------
 def run_reference(args, world):
+    """--impl reference: the reference's algorithm (the fp64 oracle port) on
+    all host cores.  A step is the whole config-2 workload (B=4 sequences of
+    T=4096 x 16 heads) when warmup + steps fit in about four minutes, else a
+    shorter T per sequence, stated in the line."""
     from oracle.parallel import OraclePool, synthetic
     pool = OraclePool()
-    # size a step so that warmup + steps stay within ~3 minutes
-    calib = synthetic(1, 64, H, K, V, seed=1)
+    calib = synthetic(1, 256, H, K, V, seed=1)
     pool.fwd_bwd(*calib)
-    t64 = min(pool.fwd_bwd(*calib) for _ in range(2))
-    budget = 150.0 / max(1, args.steps + args.warmup)
-    Ts = int(max(64, min(T, 64 * math.floor(budget / max(t64, 1e-3)))))
-    x = synthetic(1, Ts, H, K, V, seed=2)
+    t256 = min(pool.fwd_bwd(*calib) for _ in range(2))
+    per_token = t256 / 256
+    n = max(1, args.steps + args.warmup)
+    budget = 240.0 / n
+    Ts = T if B * T * per_token <= budget else int(max(256, min(T, 256 * math.floor(budget / (B * t256)))))
+    x = synthetic(B, Ts, H, K, V, seed=2)
     for _ in range(args.warmup):
         pool.fwd_bwd(*x)
     tot = 0.0
     for _ in range(args.steps):
         tot += pool.fwd_bwd(*x)
     pool.close()
-    tps = Ts * args.steps / tot
-    sample = f"one sequence of T={Ts} tokens x H=16 heads (d=128) per step, fp64 oracle port"
+    tps = B * Ts * args.steps / tot
+    sample = (f"{B} sequences of T={Ts} tokens x H=16 heads (d=128) per step"
+              f"{' (the whole config-2 workload)' if Ts == T else ''}, fp64 oracle port, heads over "
+              f"{pool.nproc} processes")
     line = {
         "metric": METRIC, "value": tps, "unit": "tokens/s", "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "config2 GDN2 op fwd+bwd (H16, d128), sampled on host cores",
-                   "seq_len_sample": Ts, "heads": H, "head_dim": K},
+        "config": {"workload": f"config2 GDN2 op fwd+bwd, B={B} H=16 T={Ts} dk=dv=128, on host cores",
+                   "global_batch": B, "seq_len": Ts, "heads": H, "head_dim": K},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": pool.nproc, "kind": "port",
                          "sample": sample},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -224,17 +334,112 @@ def run_reference(args, world):
     print(json.dumps(line), flush=True)
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline_ours():
-    """Bounded sample of config 2 through the oracle on the host cores."""
+    """The fp64 oracle port on a bounded sample of config 2 (all host cores)."""
     from oracle.parallel import OraclePool, synthetic
     pool = OraclePool()
-    x = synthetic(1, 1024, H, K, V, seed=3)
     pool.fwd_bwd(*synthetic(1, 64, H, K, V, seed=4))
-    t = pool.fwd_bwd(*x)
+    x = synthetic(1, 512, H, K, V, seed=3)
+    tot, n = 0.0, 0
+    while tot < 8.0 and n < 40:
+        tot += pool.fwd_bwd(*x)
+        n += 1
     pool.close()
-    return {"value": 1024 / t, "unit": "tokens/s", "cores": pool.nproc, "kind": "port",
-            "sample": "one sequence of T=1024 tokens x H=16 heads (d=128), fwd+bwd, fp64 oracle "
-                      f"over {pool.nproc} processes, {t:.1f} s"}
+    return {"value": 512 * n / tot, "unit": "tokens/s", "cores": pool.nproc, "kind": "port",
+            "sample": f"{n} x one sequence of T=512 tokens x H=16 heads (d=128), fwd+bwd, fp64 oracle "
+                      f"over {pool.nproc} processes, {tot:.1f} s"}
+
+
+def naive_torch_recurrence(q, k, v, g, b, w, scale):
+    """The Gated Delta Rule-2 recurrence token by token in fp32 torch, as the
+    reference's naive form (fused_recurrent_gdn2.py:193-243): autograd gives
+    the backward."""
+    import torch
+    Bn, Tn, Hn, Kn = q.shape
+    S = q.new_zeros(Bn, Hn, Kn, v.shape[-1])
+    outs = []
+    for t in range(Tn):
+        S = S * torch.exp(g[:, t])[..., None]
+        u = w[:, t] * v[:, t] - torch.einsum("bhkv,bhk->bhv", S, b[:, t] * k[:, t])
+        S = S + k[:, t][..., None] * u[:, :, None, :]
+        outs.append(torch.einsum("bhkv,bhk->bhv", S, q[:, t] * scale))
+    return torch.stack(outs, 1), S
+
+
+def cpu_baselines_torch():
+    """BASELINE B2 (naive fp32 torch recurrence with autograd, config 1 and
+    config 2 per token-head) and B4 (naive torch decode step, config 3) on
+    every host core; each sample runs for at least 5 s."""
+    import torch
+    import torch.nn.functional as F
+    ncores = os.cpu_count() or 1
+    torch.set_num_threads(ncores)
+    gen = torch.Generator().manual_seed(0)
+
+    def mk(Bn, Tn, Hn, d):
+        q = F.normalize(torch.randn(Bn, Tn, Hn, d, generator=gen), dim=-1)
+        k = F.normalize(torch.randn(Bn, Tn, Hn, d, generator=gen), dim=-1)
+        v = torch.randn(Bn, Tn, Hn, d, generator=gen)
+        b = torch.sigmoid(torch.randn(Bn, Tn, Hn, d, generator=gen))
+        w = torch.sigmoid(torch.randn(Bn, Tn, Hn, d, generator=gen))
+        g = -F.softplus(torch.randn(Bn, Tn, Hn, d, generator=gen)) * 0.1
+        do = torch.randn(Bn, Tn, Hn, d, generator=gen)
+        return [x.requires_grad_(True) for x in (q, k, v, g, b, w)], do
+
+    def time_fwd_bwd(Bn, Tn, Hn, d, min_s=5.0):
+        leaves, do = mk(Bn, Tn, Hn, d)
+        n, tot = 0, 0.0
+        while tot < min_s:
+            t0 = time.perf_counter()
+            o, _ = naive_torch_recurrence(*leaves, d ** -0.5)
+            torch.autograd.grad(o, leaves, do)
+            tot += time.perf_counter() - t0
+            n += 1
+        return tot / n, n
+
+    out = {"cores": ncores, "cpu": cpu_model(), "torch_threads": torch.get_num_threads()}
+    t1, n1 = time_fwd_bwd(1, 256, 2, 64)
+    out["b2_config1"] = {"value": 256 / t1, "unit": "tokens/s", "ms_per_step": 1e3 * t1, "repeats": n1,
+                         "sample": "config 1: B=1 H=2 T=256 d=64, naive fp32 torch recurrence, fwd + autograd bwd"}
+    t2, n2 = time_fwd_bwd(1, 256, 1, 128)
+    per_token_head = t2 / 256
+    out["b2_config2"] = {"value": 1.0 / (per_token_head * H), "unit": "tokens/s", "repeats": n2,
+                         "sample": "config 2 per token-head: B=1 H=1 T=256 d=128, naive fp32 torch, fwd + "
+                                   "autograd bwd, scaled to 16 heads per token"}
+    # B4: the config-3 decode step, in place on fp32 S [256, 16, 128, 128]
+    with torch.no_grad():
+        S = torch.randn(DEC_N, H, K, V, generator=gen) * 0.02
+        q = F.normalize(torch.randn(DEC_N, H, K, generator=gen), dim=-1)
+        k = F.normalize(torch.randn(DEC_N, H, K, generator=gen), dim=-1)
+        v = torch.randn(DEC_N, H, V, generator=gen)
+        b = torch.sigmoid(torch.randn(DEC_N, H, K, generator=gen))
+        w = torch.sigmoid(torch.randn(DEC_N, H, V, generator=gen))
+        g = -F.softplus(torch.randn(DEC_N, H, K, generator=gen)) * 0.1
+        n, tot = 0, 0.0
+        while tot < 5.0:
+            t0 = time.perf_counter()
+            S.mul_(torch.exp(g)[..., None])
+            u = w * v - torch.einsum("nhkv,nhk->nhv", S, b * k)
+            S.add_(k[..., None] * u[:, :, None, :])
+            torch.einsum("nhkv,nhk->nhv", S, q * K ** -0.5)
+            tot += time.perf_counter() - t0
+            n += 1
+    us = 1e6 * tot / n
+    out["b4_decode"] = {"value": decode_bytes_per_step(DEC_N) / (us * 1e-6) / 1e9, "unit": "GB/s",
+                        "us_per_step": us, "repeats": n,
+                        "sample": "config 3 decode step: naive torch on fp32 S [256,16,128,128] in place"}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -264,39 +469,13 @@ def load_reference_layer():
     return importlib.import_module("lit_gpt.gdn2").GatedDeltaNet2
 
 
-def run_reference_triton(args, world, rank, local):
-    if rank != 0:
-        return
-    try:
-        ref_chunk, ref_rec = load_reference_triton()
-        ref_layer = load_reference_layer() if (args.layer or args.model) else None
-    except Exception as e:  # noqa: BLE001
-        print(json.dumps({"impl": "reference-triton", "unavailable": f"{type(e).__name__}: {e}"}), flush=True)
-        return
-    if args.layer:
-        run_layer(args, 1, 0, local, layer_cls=ref_layer, impl="reference-triton")
-        return
-    if args.model:
-        run_model(args, 1, 0, local, gdn2_cls=ref_layer, impl="reference-triton")
-        return
+def measure_reference_triton(rk, steps, warmup, nb=B, nd=DEC_N):
+    """The reference's Triton op and this build's op on identical inputs on
+    this GPU: config-2 fwd+bwd and the config-3 decode step."""
     import torch
-    import torch.nn.functional as F
+    ref_chunk, ref_rec = load_reference_triton()
     gdn2 = importlib.import_module("gateddeltanet-2_b200")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    gen = torch.Generator(device=dev).manual_seed(1234)
-    nb, nd = args.batch, args.decode_seqs
-
-    def rnd(*shape):
-        return torch.randn(*shape, device=dev, generator=gen)
-
-    q = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
-    k = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
-    v = rnd(nb, T, H, V).bfloat16()
-    g = -F.softplus(rnd(nb, T, H, K)) * 0.1
-    b = torch.sigmoid(rnd(nb, T, H, K)).bfloat16()
-    w = torch.sigmoid(rnd(nb, T, H, V)).bfloat16()
-    do = rnd(nb, T, H, V).bfloat16()
+    q, k, v, g, b, w, do = config2_inputs(rk.dev, nb, H, 1234, bf16_gates=True)
     leaves = [x.requires_grad_(True) for x in (q, k, v, g, b, w)]
 
     def fwd_bwd(fn):
@@ -305,38 +484,28 @@ def run_reference_triton(args, world, rank, local):
             return torch.autograd.grad(o, leaves, do)
         return step
 
-    def timed(fn, n):
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e)
-
     arms = {"reference": fwd_bwd(ref_chunk.chunk_gdn2), "ours": fwd_bwd(gdn2.chunk_gdn2)}
-    # parity of the two arms on these inputs (max |diff| relative to max |o|)
     with torch.no_grad():
         o_r, _ = ref_chunk.chunk_gdn2(q, k, v, g, b, w)
         o_o, _ = gdn2.chunk_gdn2(q, k, v, g, b, w)
         rel = float((o_r.float() - o_o.float()).abs().max() / o_r.float().abs().max())
     res = {}
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    clocks = ClockSampler(vis.split(",")[local] if vis else local)
-    clocks.start()
     for name, fn in arms.items():
-        for _ in range(max(3, args.warmup)):
-            fn()
-        ms = timed(fn, args.steps)
-        res[name] = {"ms_per_step": ms / args.steps, "tokens_per_s": nb * T * args.steps / (ms / 1e3)}
-
-    # decode, config 3: in-place state, one token per sequence
-    S_r = rnd(nd, H, K, V) * 0.02
+        # the reference's Triton autotuner benchmarks its configurations during
+        # the first calls (minutes on a fresh box): warm up until two
+        # consecutive steps agree within 10%
+        prev, n = None, 0
+        while n < 60:
+            t = rk.timed(fn, 1)
+            n += 1
+            if n >= max(3, warmup) and prev is not None and abs(t - prev) <= 0.1 * min(t, prev):
+                break
+            prev = t
+        ms = rk.timed(fn, steps)
+        res[name] = {"ms_per_step": ms / steps, "tokens_per_s": nb * T * steps / (ms / 1e3)}
+    S_r, ring = decode_inputs(rk.dev, nd, 77)
     S_o = S_r.clone()
-    xs = (F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(), F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
-          rnd(nd, 1, H, V).bfloat16(), -F.softplus(rnd(nd, 1, H, K)) * 0.1,
-          torch.sigmoid(rnd(nd, 1, H, K)), torch.sigmoid(rnd(nd, 1, H, V)))
+    xs = ring[0]
     dec = {}
     for name, fn in (("reference", lambda: ref_rec.fused_recurrent_gdn2_fwd(*xs, initial_state=S_r,
                                                                            inplace_final_state=True)),
@@ -344,22 +513,45 @@ def run_reference_triton(args, world, rank, local):
                                                                    inplace_final_state=True))):
         for _ in range(10):
             fn()
-        ms = timed(fn, args.decode_steps)
-        us = 1e3 * ms / args.decode_steps
+        ms = rk.timed(fn, 1024)
+        us = 1e3 * ms / 1024
         dec[name] = {"us_per_step": us, "state_GBps": decode_bytes_per_step(nd) / (us * 1e-6) / 1e9}
-    clk = clocks.stop()
-    line = {
-        "metric": METRIC, "impl": "reference-triton", "value": res["reference"]["tokens_per_s"],
-        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
-        "ms_per_step": res["reference"]["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"config2: GDN2 op fwd+bwd, B={nb} H=16 T=4096 dk=dv=128; "
-                               f"config3 decode N={nd}", "gates": "b, w bf16; log-decay fp32"},
-        "source": "lit_gpt/gdn2_ops from baseline/_ref (the reference's Triton path on sm_100)",
+    return {
+        "source": "lit_gpt/gdn2_ops from baseline/_ref (the reference's Triton path on sm_100, unmodified)",
+        "config": f"config2 fwd+bwd B={nb} H=16 T=4096 d=128 (b, w bf16 in both arms); config3 decode N={nd}",
         "fwd_bwd": res, "speedup_ours_over_reference": res["ours"]["tokens_per_s"] / res["reference"]["tokens_per_s"],
         "decode": dec, "decode_speedup": dec["reference"]["us_per_step"] / dec["ours"]["us_per_step"],
-        "o_max_rel_diff": rel, "clocks": clk,
+        "o_max_rel_diff": rel,
     }
+
+
+def run_reference_triton(args, rk):
+    if rk.rank != 0:
+        return
+    rk = rk.solo()
+    try:
+        load_reference_triton()
+        ref_layer = load_reference_layer() if (args.layer or args.model) else None
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({"impl": "reference-triton", "unavailable": f"{type(e).__name__}: {e}"}), flush=True)
+        return
+    if args.layer:
+        run_layer(args, 1, 0, rk.local, layer_cls=ref_layer, impl="reference-triton")
+        return
+    if args.model:
+        rk.init_gpu()
+        print(json.dumps(measure_model(rk, args.batch, args.steps, args.warmup, gdn2_cls=ref_layer,
+                                       impl="reference-triton")), flush=True)
+        return
+    rk.init_gpu()
+    clocks = rk.clocks()
+    clocks.start()
+    r = measure_reference_triton(rk, args.steps, args.warmup, args.batch, args.decode_seqs)
+    line = {"metric": METRIC, "impl": "reference-triton", "value": r["fwd_bwd"]["reference"]["tokens_per_s"],
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": r["fwd_bwd"]["reference"]["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "clocks": clocks.stop(), **r}
     print(json.dumps(line), flush=True)
 
 
@@ -476,22 +668,19 @@ def run_layer(args, world, rank, local, layer_cls=None, impl="ours"):
 CP_T = 131072
 
 
-def run_cp(args, world, rank, local):
+def measure_cp(rk, steps, warmup):
+    """Forward of one T=131072 sequence, T split over the ranks (N=1: the
+    single-GPU forward).  Every rank also runs the single-GPU forward of the
+    whole sequence and reports how far its shard is from it."""
     import torch
-    import torch.distributed as dist
     import torch.nn.functional as F
     gdn2 = importlib.import_module("gateddeltanet-2_b200")
     from gdn2_b200 import cp
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    gen = torch.Generator(device=dev).manual_seed(5)  # the same sequence on every rank
+    world, rank = rk.world, rk.rank
+    gen = torch.Generator(device=rk.dev).manual_seed(5)  # the same sequence on every rank
 
     def rnd(*shape):
-        return torch.randn(*shape, device=dev, generator=gen)
+        return torch.randn(*shape, device=rk.dev, generator=gen)
 
     q = F.normalize(rnd(1, CP_T, H, K), dim=-1).bfloat16()
     k = F.normalize(rnd(1, CP_T, H, K), dim=-1).bfloat16()
@@ -506,244 +695,161 @@ def run_cp(args, world, rank, local):
         with torch.no_grad():
             return cp.chunk_gdn2_cp(*shard) if world > 1 else gdn2.chunk_gdn2(*shard, output_final_state=True)
 
-    def timed(fn, n):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        ms = torch.tensor([s.elapsed_time(e)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-            dist.barrier()
-        return float(ms.item())
-
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
-    ms = timed(step, args.steps)
+    ms = rk.timed(step, steps)
     o, ht = step()
     with torch.no_grad():
         o_ref, ht_ref = gdn2.chunk_gdn2(q, k, v, g, b, w, output_final_state=True)
-    err = float((o.float() - o_ref[:, rank * Ts:(rank + 1) * Ts].float()).abs().max())
-    err_t = torch.tensor([err], device=dev)
-    if world > 1:
-        dist.all_reduce(err_t, op=dist.ReduceOp.MAX)
-    st_err = float((ht - ht_ref).abs().max()) if rank == world - 1 else 0.0
-    st_t = torch.tensor([st_err], device=dev)
-    if world > 1:
-        dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
-    if rank == 0:
-        line = {
-            "metric": "config-5 context-parallel prefill tokens/s (B=1, H16, d128, T=131072)",
-            "value": CP_T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": "config5: chunk_gdn2 forward of one T=131072 sequence, T split into "
-                                   f"{world} contiguous shard(s), boundary maps all-gathered over NCCL",
-                       "global_batch": 1, "seq_len": CP_T, "heads": H, "head_dim": K,
-                       "parallelism": f"cp{world}"},
-            "o_max_abs_diff_vs_single_gpu": float(err_t.item()),
-            "final_state_max_abs_diff_vs_single_gpu": float(st_t.item()),
-        }
+    err = rk.max(float((o.float() - o_ref[:, rank * Ts:(rank + 1) * Ts].float()).abs().max()))
+    st_err = rk.max(float((ht - ht_ref).abs().max()) if rank == world - 1 else 0.0)
+    del q, k, v, g, b, w, shard, o_ref
+    return {
+        "metric": "config-5 context-parallel prefill tokens/s (B=1, H16, d128, T=131072)",
+        "value": CP_T * steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "ms_per_step": ms / steps, "scaling": "strong",
+        "workload": f"config5: forward of one T={CP_T} sequence (H=16, d=128), T split into {world} contiguous "
+                    "shard(s)" + (", boundary maps all-gathered over NCCL" if world > 1 else ""),
+        "parallelism": f"cp{world}",
+        "o_max_abs_diff_vs_single_gpu": err, "final_state_max_abs_diff_vs_single_gpu": st_err,
+    }
+
+
+def run_cp(args, rk):
+    rk.init_gpu(120)
+    r = measure_cp(rk, args.steps, args.warmup)
+    if rk.rank == 0:
+        line = {"metric": r["metric"], "value": r["value"], "unit": "tokens/s", "n_gpus": rk.world,
+                "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": r["workload"], "global_batch": 1, "seq_len": CP_T, "heads": H,
+                           "head_dim": K, "parallelism": r["parallelism"]},
+                "o_max_abs_diff_vs_single_gpu": r["o_max_abs_diff_vs_single_gpu"],
+                "final_state_max_abs_diff_vs_single_gpu": r["final_state_max_abs_diff_vs_single_gpu"]}
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    rk.close()
 
 
 # ---------------------------------------------------------------------------
 # config 4: the hybrid LM training step
 # ---------------------------------------------------------------------------
-def run_model(args, world, rank, local, gdn2_cls=None, impl="ours"):
+def measure_model(rk, nb, steps, warmup, gdn2_cls=None, impl="ours"):
     import torch
-    import torch.distributed as dist
     importlib.import_module("gateddeltanet-2_b200")
     from gdn2_b200 import _lib
     from gdn2_b200 import model as hm
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
-    nb = args.batch
+    world = rk.world if impl == "ours" else 1
     cfg = hm.HybridConfig()
     torch.manual_seed(1234)  # the same initial weights on every rank
-    net = hm.GPT(cfg, gdn2_cls=gdn2_cls).to(dev)
+    net = hm.GPT(cfg, gdn2_cls=gdn2_cls).to(rk.dev)
     net.init_weights()
     nparams = hm.num_parameters(net)
     model = net
     if world > 1:
-        model = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local], gradient_as_bucket_view=True)
+        model = torch.nn.parallel.DistributedDataParallel(net, device_ids=[rk.local], gradient_as_bucket_view=True)
     opt = torch.optim.AdamW(net.parameters(), lr=4e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
-    gen = torch.Generator(device=dev).manual_seed(99 + rank)
-    tokens = torch.randint(0, cfg.vocab_size, (nb, T + 1), device=dev, generator=gen)
+    gen = torch.Generator(device=rk.dev).manual_seed(99 + rk.rank)
+    tokens = torch.randint(0, cfg.vocab_size, (nb, T + 1), device=rk.dev, generator=gen)
     idx, tgt = tokens[:, :-1].contiguous(), tokens[:, 1:].contiguous()
 
     def step():
         return hm.train_step(model, opt, idx, tgt)
 
-    def timed(fn, n):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        ms = torch.tensor([s.elapsed_time(e)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-            dist.barrier()
-        return float(ms.item())
-
-    for _ in range(max(3, args.warmup)):
+    torch.cuda.reset_peak_memory_stats(rk.dev)
+    for _ in range(max(3, warmup)):
         loss0 = step()
     torch.cuda.synchronize()
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    clocks = ClockSampler(vis.split(",")[local] if vis else local)
-    clocks.start()
     _lib.profile_enable(True)
-    ms = timed(step, args.steps)
+    ms = rk.timed(step, steps) if world > 1 else rk.solo().timed(step, steps)
     prof = _lib.profile_read()
     _lib.profile_enable(False)
-    clk = clocks.stop()
     loss = float(step())
-    step_ms = ms / args.steps
-    ours_ms = sum(t for _, t in prof.values()) / args.steps
-    if rank == 0:
-        line = {
-            "metric": "config-4 hybrid LM training tokens/s (1.33B, GDN2 + 2048-window attention, seq 4096)",
-            "impl": impl,
-            "value": world * nb * T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": step_ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: uniform-random token ids, random-init weights",
-            "config": {"workload": f"config4: {nparams / 1e9:.2f}B hybrid LM, 24 layers (12 GatedDeltaNet2, 12 "
-                                   "sliding-window attention), d_model 2048, SwiGLU 4608, vocab 32000; fwd + "
-                                   "loss + bwd + fused AdamW step",
-                       "global_batch": nb * world, "seq_len": T, "micro_batch": nb,
-                       "parallelism": f"dp{world} (DistributedDataParallel over NCCL)" if world > 1 else "dp1",
-                       "params": nparams},
-            "clocks": clk, "gpu_launches": sum(n for n, _ in prof.values()),
-            "gdn2_kernels_ms_per_step": ours_ms,
-            "gdn2_kernels": {n: round(1e3 * t / max(c, 1), 1) for n, (c, t) in prof.items()},
-            "loss_after": loss, "loss_first_warmup": float(loss0),
-            "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
-        }
+    out = {
+        "metric": "config-4 hybrid LM training tokens/s (1.33B, GDN2 + 2048-window attention, seq 4096)",
+        "impl": impl, "value": world * nb * T * steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": max(3, warmup), "ms_per_step": ms / steps, "scaling": "weak",
+        "workload": f"config4: {nparams / 1e9:.2f}B hybrid LM, 24 layers (12 GatedDeltaNet2, 12 sliding-window "
+                    "attention), d_model 2048, SwiGLU 4608, vocab 32000; fwd + loss + bwd + fused AdamW step",
+        "global_batch": nb * world, "seq_len": T, "micro_batch": nb,
+        "parallelism": f"dp{world} (DistributedDataParallel over NCCL)" if world > 1 else "dp1", "params": nparams,
+        "gpu_launches": sum(n for n, _ in prof.values()),
+        "gdn2_kernels_ms_per_step": sum(t for _, t in prof.values()) / steps,
+        "gdn2_kernels_us_per_launch": {n: round(1e3 * t / max(c, 1), 1) for n, (c, t) in prof.items()},
+        "loss_after": loss, "loss_first_warmup": float(loss0),
+        "peak_mem_gb": torch.cuda.max_memory_allocated(rk.dev) / 1e9,
+    }
+    del model, net, opt
+    return out
+
+
+def run_model(args, rk):
+    rk.init_gpu(180)
+    clocks = rk.clocks()
+    clocks.start()
+    r = measure_model(rk, args.batch, args.steps, args.warmup)
+    clk = clocks.stop()
+    if rk.rank == 0:
+        line = {"metric": r["metric"], "impl": "ours", "value": r["value"], "unit": "tokens/s",
+                "n_gpus": rk.world, "steps": args.steps, "warmup": r["warmup"], "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic: uniform-random token ids, random-init weights",
+                "config": {k: r[k] for k in ("workload", "global_batch", "seq_len", "micro_batch", "parallelism",
+                                             "params")},
+                "clocks": clk, **{k: r[k] for k in ("gpu_launches", "gdn2_kernels_ms_per_step",
+                                                    "gdn2_kernels_us_per_launch", "loss_after",
+                                                    "loss_first_warmup", "peak_mem_gb")}}
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    rk.close()
 
 
 # ---------------------------------------------------------------------------
-def main():
-    args = parse()
-    nb, nd = args.batch, args.decode_seqs
-    dec_bytes = decode_bytes_per_step(nd)
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        if rank == 0:
-            run_reference(args, world)
-        return
-    if args.impl == "reference-triton":
-        run_reference_triton(args, world, rank, local)
-        return
-    if args.layer:
-        run_layer(args, world, rank, local)
-        return
-    if args.model:
-        run_model(args, world, rank, local)
-        return
-    if args.cp:
-        run_cp(args, world, rank, local)
-        return
+# config 2: the operator's fwd+bwd step
+# ---------------------------------------------------------------------------
+def op_step(gdn2, leaves, do):
+    o, _ = gdn2.chunk_gdn2(*leaves)
+    return torch_grad(o, leaves, do)
 
-    cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_base = cpu_baseline_ours()  # before any GPU work (spawned pool)
 
+def torch_grad(o, leaves, do):
     import torch
-    import torch.distributed as dist
-    import torch.nn.functional as F
+    return torch.autograd.grad(o, leaves, do)
+
+
+def measure_op(rk, nb, heads, steps, warmup, seed, profile=True):
+    """fwd+bwd of chunk_gdn2 on nb sequences x `heads` heads per rank; returns
+    (ms for `steps` steps (max over ranks), per-kernel profile, inputs)."""
+    import torch
     gdn2 = importlib.import_module("gateddeltanet-2_b200")
     from gdn2_b200 import _lib
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-
-    def rnd(*shape):
-        return torch.randn(*shape, device=dev, generator=gen)
-
-    q = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
-    k = F.normalize(rnd(nb, T, H, K), dim=-1).bfloat16()
-    v = rnd(nb, T, H, V).bfloat16()
-    g = -F.softplus(rnd(nb, T, H, K)) * 0.1
-    b = torch.sigmoid(rnd(nb, T, H, K))
-    w = torch.sigmoid(rnd(nb, T, H, V))
-    do = rnd(nb, T, H, V).bfloat16()
+    q, k, v, g, b, w, do = config2_inputs(rk.dev, nb, heads, seed)
     leaves = [x.requires_grad_(True) for x in (q, k, v, g, b, w)]
 
     def step():
-        o, _ = gdn2.chunk_gdn2(*leaves)
-        return torch.autograd.grad(o, leaves, do)
+        return op_step(gdn2, leaves, do)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def timed(fn, n):
-        barrier()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        ms = torch.tensor([s.elapsed_time(e)], device=dev)
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        barrier()
-        return float(ms.item())
-
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     torch.cuda.synchronize()
+    if profile:
+        _lib.profile_enable(True)
+    ms = rk.timed(step, steps)
+    prof = _lib.profile_read() if profile else {}
+    if profile:
+        _lib.profile_enable(False)
+    return ms, prof, (q, k, v, g, b, w, do)
 
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    clocks = ClockSampler(vis.split(",")[local] if vis else local)
-    clocks.start()
-    _lib.profile_enable(True)
-    ms = timed(step, args.steps)
-    prof = _lib.profile_read()
-    _lib.profile_enable(False)
-    clk = clocks.stop()
-    gpu_launches = sum(n for n, _ in prof.values())
-    tok_per_step = world * nb * T
-    value = tok_per_step * args.steps / (ms / 1e3)
 
-    # ---- end to end through the public API: pinned host inputs -> device ----
-    # Every step copies its own inputs and cotangent from pinned host memory
-    # inside the timed region.  Two device buffer sets: step i+1's copy runs on
-    # a second stream while step i computes (what a data loader with prefetch
-    # does); a step waits only for its own copy.
-    host = [x.detach().cpu().pin_memory() for x in (q, k, v, g, b, w, do)]
-    sets = [[torch.empty_like(x) for x in (q, k, v, g, b, w, do)] for _ in range(2)]
-    copy_stream = torch.cuda.Stream(device=dev)
+def measure_e2e(rk, tensors, tok_per_step, steps):
+    """The strong-split step through chunk_gdn2 with this rank's inputs and
+    cotangent copied from pinned host memory inside the timed region (two
+    device buffer sets: step i+1's copy runs on a second stream while step i
+    computes) and the loss scalar read back."""
+    import torch
+    gdn2 = importlib.import_module("gateddeltanet-2_b200")
+    host = [x.detach().cpu().pin_memory() for x in tensors]
+    sets = [[torch.empty_like(x) for x in tensors] for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device=rk.dev)
     copied = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     for ev in consumed:
@@ -758,7 +864,7 @@ def main():
                 d.copy_(hsrc, non_blocking=True)
             copied[sl].record(copy_stream)
 
-    def e2e_run(n):
+    def run(n):
         copy_stream.wait_stream(torch.cuda.current_stream())  # copies start inside the timed region
         issue_copy(0)
         for i in range(n):
@@ -776,24 +882,21 @@ def main():
             for d in bufs[:6]:
                 d.requires_grad_(False)
 
-    n_e2e = max(3, min(args.steps, 20))
-    e2e_run(2)
-    e2e_ms = timed(lambda: e2e_run(n_e2e), 1)
+    n = max(3, min(steps, 20))
+    run(2)
+    ms = rk.timed(lambda: run(n), 1)
     h2d = sum(x.numel() * x.element_size() for x in host)
-    e2e = {"value": tok_per_step * n_e2e / (e2e_ms / 1e3), "unit": "tokens/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": n_e2e,
-           "path": "chunk_gdn2 fwd+bwd; each step's inputs and cotangent copied from pinned host "
-                   "memory inside the timed region (double-buffered: the next step's copy overlaps "
-                   "this step's compute), loss scalar read back"}
+    return {"value": tok_per_step * n / (ms / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d * rk.world, "d2h_bytes_per_step": 4 * rk.world, "steps": n,
+            "path": "chunk_gdn2 fwd+bwd of each rank's heads; every step's inputs and cotangent copied from "
+                    "pinned host memory inside the timed region (double-buffered: the next step's copy overlaps "
+                    "this step's compute), loss scalar read back; bytes summed over the ranks"}
 
-    # ---- decode (config 3): in-place state update, 1 token per sequence --------
-    S = rnd(nd, H, K, V) * 0.02
-    ring = []
-    for i in range(4):
-        ring.append((F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
-                     F.normalize(rnd(nd, 1, H, K), dim=-1).bfloat16(),
-                     rnd(nd, 1, H, V).bfloat16(), -F.softplus(rnd(nd, 1, H, K)) * 0.1,
-                     torch.sigmoid(rnd(nd, 1, H, K)), torch.sigmoid(rnd(nd, 1, H, V))))
+
+def measure_decode(rk, nd, steps):
+    gdn2 = importlib.import_module("gateddeltanet-2_b200")
+    from gdn2_b200 import _lib
+    S, ring = decode_inputs(rk.dev, nd, 4321 + rk.rank)
     it = [0]
 
     def dec_step():
@@ -804,57 +907,181 @@ def main():
     for _ in range(10):
         dec_step()
     _lib.profile_enable(True)
-    dec_ms = timed(dec_step, args.decode_steps)
-    dprof = _lib.profile_read()
+    ms = rk.timed(dec_step, steps)
+    prof = _lib.profile_read()
     _lib.profile_enable(False)
+    return ms, prof
+
+
+_T0 = time.perf_counter()
+
+
+def note(msg):
+    """Progress of the run on stderr (section and elapsed seconds)."""
+    print(f"[bench {time.perf_counter() - _T0:7.1f} s] {msg}", file=sys.stderr, flush=True)
+
+
+def dominant(prof):
+    """The kernel with the largest device time among those with known bytes."""
+    known = {n: v for n, v in prof.items() if n in KERNEL_BYTES_PER_TOKEN_HEAD}
+    return max(known.items(), key=lambda kv: kv[1][1]) if known else None
+
+
+def main():
+    args = parse()
+    rk = Ranks()
+    if args.impl == "reference":
+        if rk.rank == 0:
+            run_reference(args, rk.world)
+        return
+    if args.impl == "reference-triton":
+        run_reference_triton(args, rk)
+        return
+    if args.layer:
+        run_layer(args, rk.world, rk.rank, rk.local)
+        return
+    if args.model:
+        run_model(args, rk)
+        return
+    if args.cp:
+        run_cp(args, rk)
+        return
+
+    world, rank = rk.world, rk.rank
+    nb, nd_total = args.batch, args.decode_seqs
+    full = nb == B and nd_total == DEC_N
+    cpu_base = cpu_torch = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        note("cpu baseline: oracle port")
+        cpu_base = cpu_baseline_ours()  # before any GPU work (spawned pool)
+        note("cpu baselines: naive torch")
+        cpu_torch = cpu_baselines_torch()
+
+    import torch
+    rk.init_gpu(180)
     peak, peak_kind = peaks()
+
+    # ---- config 2, strong split of the 64 (sequence, head) pairs ----------------
+    note("config 2")
+    strong = H % world == 0
+    heads = H // world if strong else H
+    clocks = rk.clocks()
+    clocks.start()
+    ms, prof, tensors = measure_op(rk, nb, heads, args.steps, args.warmup, 1234 + rank)
+    clk = clocks.stop()
+    tok_per_step = nb * T if strong else world * nb * T
+    value = tok_per_step * args.steps / (ms / 1e3)
+    gpu_launches = sum(n for n, _ in prof.values())
+
+    dom = dominant(prof)
+    roofline = None
+    if dom is not None:
+        name, (nl, tms) = dom
+        per_launch_s = tms / nl / 1e3
+        alg = KERNEL_BYTES_PER_TOKEN_HEAD[name] * nb * T * heads
+        achieved = alg / per_launch_s / 1e9
+        tot_ms = sum(x[1] for x in prof.values())
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "peak_source": peak_kind,
+                    "traffic": traffic_table().get(name) if (full and world == 1) else None, "kernel": name,
+                    "algorithmic_bytes_per_launch": alg, "us_per_launch": per_launch_s * 1e6,
+                    "kernel_shares": {n: round(t / tot_ms, 4) for n, (c, t) in prof.items()},
+                    "kernel_us_per_step": {n: round(1e3 * t / args.steps, 1) for n, (c, t) in prof.items()}}
+    # op level: SURVEY's 7,456 algorithmic bytes per token-head for fwd+bwd
+    op_bytes = 7456 * H * tok_per_step
+    op_achieved = op_bytes * args.steps / (ms / 1e3) / 1e9
+    op_roofline = {"bound": "hbm", "achieved": op_achieved, "peak": peak * world, "unit": "GB/s",
+                   "frac": op_achieved / (peak * world), "peak_source": peak_kind,
+                   "algorithmic_bytes_per_step": op_bytes,
+                   "note": "whole op (all kernels), 7456 B per token-head fwd+bwd, peak summed over the GPUs"}
+
+    weak = None
+    if world > 1:
+        wms, _, _ = measure_op(rk, B, H, args.steps, args.warmup, 999 + rank, profile=False)
+        weak = {"value": world * B * T * args.steps / (wms / 1e3), "unit": "tokens/s",
+                "ms_per_step": wms / args.steps, "global_batch": B * world, "scaling": "weak",
+                "workload": f"config2 with B=4 x 16 heads on each of the {world} ranks"}
+
+    note("config 2 end to end")
+    e2e = measure_e2e(rk, tensors, tok_per_step, args.steps)
+    del tensors
+
+    # ---- config 3 decode, split by sequence ------------------------------------
+    note("config 3")
+    nd = nd_total // world if nd_total % world == 0 else nd_total
+    dec_ms, dprof = measure_decode(rk, nd, args.decode_steps)
     dec_us = 1e3 * dec_ms / args.decode_steps
-    dec_gbs = dec_bytes / (dec_us * 1e-6) / 1e9
+    dec_total = nd * world
+    dec_gbs = decode_bytes_per_step(dec_total) / (dec_us * 1e-6) / 1e9
     dk = dprof.get("recurrent_kernel", (1, dec_ms))
     dk_us = 1e3 * dk[1] / max(dk[0], 1)
-    decode = {"metric": "decode-step state HBM GB/s", "value": world * dec_gbs, "unit": "GB/s",
-              "us_per_step": dec_us, "tokens_per_s": world * nd / (dec_us * 1e-6),
-              "config": {"workload": "config3 decode step", "sequences_per_gpu": nd, "heads": H,
-                         "state": f"fp32 [{nd},16,128,128] in place", "steps": args.decode_steps},
-              "roofline": {"bound": "hbm", "achieved": dec_bytes / (dk_us * 1e-6) / 1e9,
+    decode = {"metric": "decode-step state HBM GB/s", "value": dec_gbs, "unit": "GB/s",
+              "us_per_step": dec_us, "tokens_per_s": dec_total / (dec_us * 1e-6),
+              "scaling": "strong" if nd * world == nd_total else "weak",
+              "config": {"workload": "config3 decode step", "sequences": dec_total, "sequences_per_gpu": nd,
+                         "heads": H, "state": f"fp32 [{dec_total},16,128,128] in place", "steps": args.decode_steps},
+              "roofline": {"bound": "hbm", "achieved": decode_bytes_per_step(nd) / (dk_us * 1e-6) / 1e9,
                            "peak": peak, "unit": "GB/s",
-                           "frac": dec_bytes / (dk_us * 1e-6) / 1e9 / peak,
-                           "peak_source": peak_kind, "kernel": "recurrent_kernel",
-                           "us_per_launch": dk_us,
-                           "traffic": traffic_table().get("recurrent_kernel") if nd == DEC_N else None}}
+                           "frac": decode_bytes_per_step(nd) / (dk_us * 1e-6) / 1e9 / peak,
+                           "peak_source": peak_kind, "kernel": "recurrent_kernel", "us_per_launch": dk_us,
+                           "traffic": traffic_table().get("recurrent_kernel") if (nd == DEC_N) else None}}
+    if cpu_torch is not None:
+        decode["cpu_baseline"] = {"value": cpu_torch["b4_decode"]["value"], "unit": "GB/s",
+                                  "cores": cpu_torch["cores"], "kind": "port",
+                                  "sample": cpu_torch["b4_decode"]["sample"]}
+    torch.cuda.empty_cache()
 
-    # ---- roofline of the dominant kernel of the fwd+bwd step ------------------
-    dom = max(prof.items(), key=lambda kv: kv[1][1])
-    name, (nl, tms) = dom
-    per_launch_s = tms / nl / 1e3
-    alg = KERNEL_BYTES_PER_TOKEN_HEAD[name] * nb * T * H
-    achieved = alg / per_launch_s / 1e9
-    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_kind,
-                "traffic": traffic_table().get(name) if nb == B else None, "kernel": name,
-                "algorithmic_bytes_per_launch": alg, "us_per_launch": per_launch_s * 1e6,
-                "kernel_shares": {n: round(t / sum(x[1] for x in prof.values()), 4)
-                                  for n, (c, t) in prof.items()}}
+    # ---- config 5 (CP prefill) and config 4 (model) --------------------------
+    extras = {}
+    if full:
+        note("config 5")
+        try:
+            extras["cp"] = measure_cp(rk, 5, 3)
+        except Exception as e:  # noqa: BLE001
+            extras["cp"] = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+        note("config 4")
+        try:
+            extras["model"] = measure_model(rk, 4, 5, 3)
+        except Exception as e:  # noqa: BLE001
+            extras["model"] = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+        if world == 1 and not args.no_reference_triton:
+            note("reference Triton op")
+            try:
+                extras["reference_triton"] = measure_reference_triton(rk, min(args.steps, 20), args.warmup)
+                torch.cuda.empty_cache()
+            except Exception as e:  # noqa: BLE001
+                extras["reference_triton"] = {"unavailable": f"{type(e).__name__}: {e}"}
 
+    note("done")
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic",
-            "config": {"workload": f"config2: GDN2 op fwd+bwd, B={nb} H=16 T=4096 dk=dv=128 chunk 64 per GPU",
-                       "global_batch": nb * world, "seq_len": T, "heads": H, "head_dim": K,
-                       "parallelism": f"(batch x head) shards, {world} GPU(s), no collectives",
-                       "l2": f"inputs {0.15 * nb:.2f} GB per GPU per step (> 126 MB L2), no flush needed",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"config2: GDN2 op fwd+bwd, B={nb} H=16 T=4096 dk=dv=128 chunk 64, "
+                                   + (f"the 64 (sequence, head) pairs split over {world} GPU(s), "
+                                      f"{nb * heads} per GPU" if strong else f"B={nb} x 16 heads per GPU"),
+                       "global_batch": nb, "seq_len": T, "heads": H, "head_dim": K,
+                       "heads_per_gpu": heads,
+                       "parallelism": f"(batch x head) shards over {world} GPU(s), no collectives",
+                       "l2": f"inputs {0.15 * nb * heads / H:.2f} GB per GPU per step "
+                             f"({'>' if 0.15 * nb * heads / H > 0.126 else '<'} 126 MB L2), no flush",
                        "gates": "b, w, log-decay fp32; q, k, v bf16"},
             "clocks": clk, "e2e": e2e, "gpu_launches": gpu_launches, "roofline": roofline,
-            "decode": decode,
+            "op_roofline": op_roofline, "decode": decode,
         }
+        if weak is not None:
+            line["weak"] = weak
+        line.update(extras)
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
+        if cpu_torch is not None:
+            line["cpu_baselines"] = cpu_torch
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    rk.close()
 
 
 if __name__ == "__main__":

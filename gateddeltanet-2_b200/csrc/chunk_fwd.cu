@@ -830,6 +830,8 @@ int launch_transition_kv(const gdn2_chunk_args& a, const ChunkWs& ws, float* map
     k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, sm_count());
     GDN2_LAUNCH_CHECK();
   }
+  // d_k = d_v = 128: the tcgen05 scan, one CTA for the M columns and one for h_e
+  if (scan_fwd_tc_supported(a)) return scan_trans_tc_launch(a, ws, maps, s);
   const size_t sm2 = sizeof(ScanSmem<K>);
   GDN2_CUDA_TRY(cudaFuncSetAttribute(chunk_scan_fwd_kernel<K, V, true>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2));

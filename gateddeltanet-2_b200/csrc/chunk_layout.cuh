@@ -20,14 +20,61 @@ struct ChunkWs {
   __nv_bfloat16* qg;   // scale q 2^G           [tokens, H, K]
   __nv_bfloat16* v_new;// [tokens, H, V]
   __nv_bfloat16* h;    // per-chunk entering state, transposed: [NT, H, V, K]
+  float* segX;         // segmented scan: segment states [N*H, nseg, K, V] fp32 (or nullptr)
+  float* segM;         // segmented scan: segment transitions [N*H, nseg, K, K] fp32 (kept for the backward)
 };
 
 struct BwdWs {
   __nv_bfloat16* dh;   // state cotangent at the end of each chunk, transposed [NT, H, V, K]
   __nv_bfloat16* dvn;  // cotangent of v_new [tokens, H, V]
+  float* segZ;         // segmented reverse scan: segment state cotangents [N*H, nseg, K, V] fp32
 };
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+// How the tcgen05 scans cut each sequence into segments (scan_tc.cu).  With
+// one CTA per (sequence, head) a scan walks every chunk of its sequence in
+// series, so with few pairs per GPU most SMs idle.  Cutting a sequence into
+// nseg segments runs the scans in three launches (segment transitions, an
+// fp32 fold, the segments from their entering states): more CTAs in flight,
+// about twice the scan work.  The plan minimises a cost in microseconds
+// measured on B200 (one resident scan CTA per SM, 148 SMs): a chunk step of
+// a scan CTA ~3.3 us, a scan launch ~8 us of fixed cost, a serial fold step
+// ~2 us per wave of fold CTAs (16 per pair) plus ~5 us per fold launch.
+// Dense batches of d_k = d_v = 128 with at least 32 chunks per sequence only;
+// the result depends on the arguments alone, so the forward, the backward
+// and the workspace queries agree.
+struct SegPlan {
+  int nseg;     // segments per sequence (1: no segmentation)
+  int seg_len;  // chunks per segment
+};
+constexpr int kPlanSms = 148;
+constexpr int kSegMinChunks = 32;
+constexpr int kFoldCtasPerPair = 16;
+
+inline SegPlan seg_plan(const gdn2_chunk_args& a) {
+  const int64_t nts = (a.T + 63) / 64;
+  SegPlan p{1, (int)nts};
+  if (a.K != 128 || a.V != 128 || a.cu_seqlens || a.N <= 0 || nts < kSegMinChunks) return p;
+  const int64_t NH = a.N * a.H;
+  auto waves = [](int64_t ctas) { return (double)((ctas + kPlanSms - 1) / kPlanSms); };
+  constexpr double kStep = 3.3, kPass = 8.0, kFoldStep = 2.0, kFoldLaunch = 5.0;
+  const double base = waves(NH) * (double)nts * kStep + kPass;
+  double best = base;
+  SegPlan cand = p;
+  for (int64_t n = 3; n <= 64; ++n) {
+    const int64_t L = (nts + n - 1) / n;
+    const int64_t nn = (nts + L - 1) / L;  // segments actually formed
+    if (nn < 3 || L < 2) continue;
+    const double cost = (waves(NH * (2 * nn - 3)) + waves(NH * (nn - 1))) * (double)L * kStep + 2 * kPass +
+                        waves(NH * kFoldCtasPerPair) * (double)(nn - 2) * kFoldStep + kFoldLaunch;
+    if (cost < best) {
+      best = cost;
+      cand = SegPlan{(int)nn, (int)L};
+    }
+  }
+  return best < 0.85 * base ? cand : p;
+}
 
 // Carves `base` (or computes the size when base == nullptr).
 inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws) {
@@ -63,6 +110,12 @@ inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws)
     w.qn = (__nv_bfloat16*)a.q;
     w.kn = (__nv_bfloat16*)a.k;
   }
+  const SegPlan plan = seg_plan(a);
+  if (plan.nseg > 1) {
+    const size_t nsl = (size_t)a.N * H * (size_t)plan.nseg;
+    w.segX = (float*)take(nsl * K * V * 4);
+    w.segM = (float*)take(nsl * K * K * 4);
+  }
   if (ws) *ws = w;
   return off;
 }
@@ -79,6 +132,8 @@ inline size_t bwd_ws_layout(const gdn2_chunk_args& a, void* base, BwdWs* ws) {
   BwdWs w{};
   w.dh = (__nv_bfloat16*)take((size_t)a.NT * H * K * V * 2);
   w.dvn = (__nv_bfloat16*)take(tok * H * V * 2);
+  const SegPlan plan = seg_plan(a);
+  if (plan.nseg > 1) w.segZ = (float*)take((size_t)a.N * H * (size_t)plan.nseg * K * V * 4);
   if (ws) *ws = w;
   return off;
 }
@@ -97,6 +152,8 @@ bool scan_fwd_tc_supported(const gdn2_chunk_args& a);
 int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
 int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
                        cudaStream_t s);
+// context-parallel transition [M | h_e] of a dense shard on the tcgen05 scan (d_k = d_v = 128)
+int scan_trans_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s);
 int tc_fault_read(int clear, unsigned int* out);
 // fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up
 int layer_fault_read(int clear, unsigned int* out);

@@ -45,6 +45,29 @@ def test_workspace_sizes(gdn2):
     assert lib.gdn2_chunk_bwd_workspace_size(_args(gdn2)) == 256 * 16 * 128 * 128 * 2 + tok * 128 * 2
 
 
+def test_segmented_scan_workspace(gdn2):
+    """Few (sequence, head) pairs over a long sequence: the plan cuts the scans
+    into segments and the workspaces grow by the segment states and
+    transitions (fp32 [N*H, nseg, 128, 128] each; the backward one more)."""
+    lib = gdn2._lib.load()
+    seg = _args(gdn2, B=1, N=1, H=2, NT=33, T=2100)
+    tok, nh = 2100 * 2, 2
+    plain = lib.gdn2_chunk_bwd_workspace_size(_args(gdn2, B=1, N=1, H=2, NT=16, T=1000))
+    assert plain == 16 * 2 * 128 * 128 * 2 + 1000 * 2 * 128 * 2  # 16 chunks: one segment
+    fwd, bwd = lib.gdn2_chunk_workspace_size(seg), lib.gdn2_chunk_bwd_workspace_size(seg)
+    per = nh * 128 * 128 * 4
+    # 11 segments of 3 chunks
+    assert bwd == 33 * nh * 128 * 128 * 2 + tok * 128 * 2 + 11 * per
+    assert fwd >= 2 * 11 * per
+    # many pairs (config 2): one CTA per pair fills the GPU, no segments
+    assert lib.gdn2_chunk_bwd_workspace_size(_args(gdn2)) == 256 * 16 * 128 * 128 * 2 + 4 * 4096 * 16 * 128 * 2
+    # the chunk states buffer is found through the offset query
+    off = lib.gdn2_chunk_workspace_offset(seg, gdn2._lib.WS_CHUNK_STATES)
+    assert 0 < off < fwd and off % 256 == 0
+    nosave = _args(gdn2, B=1, N=1, H=2, NT=33, T=2100, flags=0)
+    assert lib.gdn2_chunk_workspace_offset(nosave, gdn2._lib.WS_CHUNK_STATES) == 2 ** 64 - 1
+
+
 @pytest.mark.parametrize("kw,code", [
     (dict(K=96), 4), (dict(V=32), 4), (dict(dtype_qkv=1), 3), (dict(NT=255), 2),
     (dict(N=3), 2), (dict(flags=4), 7),

@@ -241,6 +241,67 @@ def test_intermediate_states_match_oracle_prefix_states(gdn2, K, V, transpose):
         np.testing.assert_allclose(got, ref, rtol=2e-3 + 2 ** -8, atol=1e-2, err_msg=f"h[{c}]")
 
 
+# Segmented scans (few (sequence, head) pairs, at least 32 chunks per sequence):
+# the workspace plan cuts each sequence into segments, the scans run as
+# segment transitions + an fp32 fold + the segments from their entering
+# states.  B=1, H=2, T=2100 gives 11 segments of 3 chunks (the last chunk
+# holds 52 tokens).
+@pytest.mark.parametrize("B,T,H", [(1, 2100, 2), (2, 2048, 1)])
+def test_segmented_scan_matches_oracle(gdn2, B, T, H):
+    K = V = 128
+    q, k, v, gg, b, w = _inputs(T + H, B, T, H, K, V)
+    h0 = torch.randn(B, H, K, V, generator=torch.Generator().manual_seed(T)) * 0.1
+    _bwd_vs_oracle(gdn2, q, k, v, gg, b, w, h0=h0, seed=T)
+
+
+def test_segmented_scan_gate_l2norm_transposed_state(gdn2):
+    """Segments with the gate and l2norm in the kernel and [V, K] states."""
+    B, T, H, K, V = 1, 2300, 1, 128, 128
+    q, k, v, gg, b, w = _inputs(31, B, T, H, K, V, bw=torch.bfloat16)
+    g2 = torch.Generator().manual_seed(6)
+    graw = torch.randn(B, T, H, K, generator=g2)
+    A_log = torch.rand(H, generator=g2) * 2.0
+    dt_bias = torch.randn(H * K, generator=g2) * 0.5
+    h0 = torch.randn(B, H, K, V, generator=g2) * 0.1
+    do = torch.randn(B, T, H, V, generator=g2).bfloat16()
+    dht = torch.randn(B, H, K, V, generator=g2) * 0.1
+    leaves = [x.cuda().requires_grad_(True) for x in (q, k, v, graw, b, w)]
+    h0T = h0.transpose(-1, -2).contiguous().cuda().requires_grad_(True)
+    A_d, dt_d = A_log.cuda().requires_grad_(True), dt_bias.cuda().requires_grad_(True)
+    o, htT = gdn2.chunk_gdn2(*leaves, initial_state=h0T, output_final_state=True,
+                             use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
+                             transpose_state_layout=True, A_log=A_d, dt_bias=dt_d)
+    torch.autograd.backward([o, htT], [do.cuda(), dht.transpose(-1, -2).contiguous().cuda()])
+    torch.cuda.synchronize()
+    r = orc.chunk_gdn2(*(x.float().numpy() for x in (q, k, v, graw, b, w)), initial_state=h0.numpy(),
+                       output_final_state=True, use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
+                       A_log=A_log.numpy(), dt_bias=dt_bias.numpy(), do=do.float().numpy(), dht=dht.numpy())
+    assert_close(o, r.o, "o")
+    assert_close(htT.transpose(-1, -2), r.final_state, "ht")
+    for n, leaf in zip("qkvgbw", leaves):
+        assert_close(leaf.grad, r.grads[n], f"d{n}")
+    assert_close(h0T.grad.transpose(-1, -2), r.grads["h0"], "dh0")
+    mA, mdt = gate_param_masses(graw, dt_bias, r.grads["g"], H)
+    assert_close_reduced(A_d.grad, r.grads["A_log"], mA, "dA_log", rtol=RTOL_SUM)
+    assert_close_reduced(dt_d.grad, r.grads["dt_bias"], mdt, "ddt_bias", rtol=RTOL_SUM)
+
+
+def test_segmented_intermediate_states(gdn2):
+    """return_intermediate_states when the forward scan runs in segments: the
+    chunk states come from the segment passes."""
+    B, T, H, K, V = 1, 2100, 1, 128, 128
+    q, k, v, gg, b, w = _inputs(17, B, T, H, K, V)
+    with torch.inference_mode():
+        _, _, hs = gdn2.chunk_gdn2(q.cuda(), k.cuda(), v.cuda(), gg.cuda(), b.cuda(), w.cuda(),
+                                   output_final_state=True, return_intermediate_states=True)
+    torch.cuda.synchronize()
+    x = [t.float().numpy() for t in (q, k, v, gg, b, w)]
+    for c in (1, 2, 3, 4, 6, 17, 29, 30, 31, 32):  # around segment boundaries (3 chunks each)
+        _, ref, _ = orc.recurrent_fwd(*(t[:, :64 * c] for t in x), K ** -0.5)
+        np.testing.assert_allclose(hs[:, c].float().cpu().numpy(), ref, rtol=2e-3 + 2 ** -8, atol=1e-2,
+                                   err_msg=f"h[{c}]")
+
+
 def test_no_bounded_wait_gave_up(gdn2):
     """The tensor-core kernels run above bound every barrier wait; none of
     them may have given up (that would mean invalid results above)."""
