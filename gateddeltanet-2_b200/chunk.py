@@ -50,7 +50,7 @@ def _make_args(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, ht, o, fl
         B=B, T=T, H=H, K=K, V=V, N=N, NT=NT,
         cu_seqlens=_lib.ptr(cu), chunk_index=_lib.ptr(cidx), chunk_offset=_lib.ptr(coff),
         scale=float(scale), lower_bound=float(lower_bound if lower_bound is not None else 0.0),
-        flags=flags, dtype_qkv=_lib.BF16,
+        flags=flags, dtype_qkv=_lib.F32 if q.dtype == torch.float32 else _lib.BF16,
         dtype_bw=_lib.BF16 if b.dtype == torch.bfloat16 else _lib.F32,
         q=_lib.ptr(q), k=_lib.ptr(k), v=_lib.ptr(v), g=_lib.ptr(g), b=_lib.ptr(b), w=_lib.ptr(w),
         A_log=_lib.ptr(A_log), dt_bias=_lib.ptr(dt_bias), h0=_lib.ptr(initial_state),
@@ -66,10 +66,14 @@ def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, outpu
     the backward's operands in the workspace)."""
     _lib.require_device(q)
     dtypes = (q.dtype, k.dtype, v.dtype, g.dtype, b.dtype, w.dtype)
-    bw = _bw_dtype(b, w)
-    qb, kb, vb = (x.to(torch.bfloat16).contiguous() for x in (q, k, v))
-    # bf16 g (the layer's gate pre-activation) is read as is; anything else as fp32
-    gf = g.contiguous() if g.dtype == torch.bfloat16 else g.to(torch.float32).contiguous()
+    # fp32 q: the fp32 path (every input in fp32, the recurrence in fp32);
+    # otherwise the bf16 tensor-core path with fp32 accumulation
+    fp32 = q.dtype == torch.float32
+    cdt = torch.float32 if fp32 else torch.bfloat16
+    bw = torch.float32 if fp32 else _bw_dtype(b, w)
+    qb, kb, vb = (x.to(cdt).contiguous() for x in (q, k, v))
+    # bf16 g (the layer's gate pre-activation) is read as is on the bf16 path; anything else as fp32
+    gf = g.contiguous() if (g.dtype == torch.bfloat16 and not fp32) else g.to(torch.float32).contiguous()
     bb, wb = b.to(bw).contiguous(), w.to(bw).contiguous()
     A_log_f = A_log.float().contiguous() if (use_gate_in_kernel and A_log is not None) else None
     dt_f = dt_bias.float().contiguous() if (use_gate_in_kernel and dt_bias is not None) else None
@@ -99,7 +103,7 @@ def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, outpu
         flags |= _lib.HAS_H0
     if save:
         flags |= _lib.SAVE_FOR_BWD
-    o = torch.empty(B, T, H, V, device=q.device, dtype=torch.bfloat16)
+    o = torch.empty(B, T, H, V, device=q.device, dtype=cdt)
     ht = None
     if output_final_state:
         shp = (N, H, V, K) if transpose_state_layout else (N, H, K, V)
@@ -113,7 +117,7 @@ def _chunk_forward(q, k, v, g, b, w, A_log, dt_bias, scale, initial_state, outpu
     with torch.cuda.device(q.device):
         _lib.check(lib.gdn2_chunk_fwd(args, ws.data_ptr(), ws_bytes, _lib.stream_ptr(q.device)),
                    "gdn2_chunk_fwd")
-    o_out = o if dtypes[0] == torch.bfloat16 else o.to(dtypes[0])
+    o_out = o if dtypes[0] == cdt else o.to(dtypes[0])
     saved = (qb, kb, vb, gf, bb, wb, A_log_f, dt_f, h0, ws, cu, cidx, coff)
     meta = (flags, float(scale), lb, N, NT, ws_bytes, dtypes,
             A_log.dtype if A_log is not None else None,
@@ -137,7 +141,7 @@ def _chunk_backward(saved, meta, do, dht, state_only=False):
     if state_only:
         bflags |= _lib.BWD_STATE_ONLY
     args = _make_args(qb, kb, vb, gf, bb, wb, A_log_f, dt_f, scale, h0, None, None, bflags, lb, geom)
-    dob = do.to(torch.bfloat16).contiguous()
+    dob = do.to(qb.dtype).contiguous()
     dht_f = dht.to(torch.float32).contiguous() if dht is not None else None
     tr = bool(flags & _lib.TRANSPOSE_STATE)
     if state_only:
@@ -209,9 +213,14 @@ def _intermediate_states(ws, args, B, T, H, K, V, NT, transpose):
     off = _lib.load().gdn2_chunk_workspace_offset(args, _lib.WS_CHUNK_STATES)
     if off == 2 ** 64 - 1:
         raise RuntimeError("the forward workspace keeps no chunk states for these arguments")
-    # the workspace keeps each chunk state transposed, [NT, H, V, K]
-    hT = ws[off:off + NT * H * K * V * 2].view(torch.bfloat16).view(NT, H, V, K)
-    h = (hT if transpose else hT.transpose(-1, -2)).contiguous()
+    if args.dtype_qkv == _lib.F32:
+        # the fp32 path keeps them in fp32, [NT, H, K, V]
+        hs = ws[off:off + NT * H * K * V * 4].view(torch.float32).view(NT, H, K, V)
+        h = (hs.transpose(-1, -2) if transpose else hs).contiguous()
+    else:
+        # the bf16 path keeps each chunk state transposed, [NT, H, V, K]
+        hT = ws[off:off + NT * H * K * V * 2].view(torch.bfloat16).view(NT, H, V, K)
+        h = (hT if transpose else hT.transpose(-1, -2)).contiguous()
     if args.cu_seqlens is None:
         return h.view(B, NT // max(B, 1), H, *h.shape[-2:])
     return h.unsqueeze(0)

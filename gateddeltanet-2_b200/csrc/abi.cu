@@ -13,7 +13,13 @@ int check_chunk(const gdn2_chunk_args* a, bool need_ptrs = true, bool need_out =
   if (!a) return GDN2_ERR_NULL_POINTER;
   if (a->B < 0 || a->T < 0 || a->H <= 0 || a->N < 0 || a->NT < 0) return GDN2_ERR_SHAPE;
   if (!dim_ok(a->K) || !dim_ok(a->V)) return GDN2_ERR_UNSUPPORTED_DIM;
-  if (a->dtype_qkv != GDN2_BF16) return GDN2_ERR_DTYPE;
+  if (a->dtype_qkv == GDN2_F32) {
+    // the fp32 path takes every input in fp32 and has no separate intra stage
+    if (a->dtype_bw != GDN2_F32 || (a->flags & GDN2_G_BF16)) return GDN2_ERR_DTYPE;
+    if (a->flags & GDN2_SKIP_INTRA) return GDN2_ERR_FLAGS;
+  } else if (a->dtype_qkv != GDN2_BF16) {
+    return GDN2_ERR_DTYPE;
+  }
   if (a->dtype_bw != GDN2_BF16 && a->dtype_bw != GDN2_F32) return GDN2_ERR_DTYPE;
   if (a->cu_seqlens) {
     if (a->B != 1 || !a->chunk_index || !a->chunk_offset) return GDN2_ERR_SHAPE;
@@ -91,6 +97,8 @@ size_t gdn2_chunk_workspace_offset(const gdn2_chunk_args* a, int which) {
   chunk_ws_layout(*a, base, &ws);
   switch (which) {
     case GDN2_WS_CHUNK_STATES:
+      if (a->dtype_qkv == GDN2_F32)
+        return ws.ckpt ? (size_t)(reinterpret_cast<char*>(ws.ckpt) - base) : ~size_t(0);
       return ws.h ? (size_t)(reinterpret_cast<char*>(ws.h) - base) : ~size_t(0);
     default: return ~size_t(0);
   }
@@ -109,6 +117,7 @@ int gdn2_chunk_fwd(const gdn2_chunk_args* a, void* workspace, size_t workspace_b
   if (a->N == 0 || a->B * a->T == 0) return GDN2_OK;
   ChunkWs ws;
   chunk_ws_layout(*a, workspace, &ws);
+  if (a->dtype_qkv == GDN2_F32) return chunk_fwd_fp32_launch(*a, ws, reinterpret_cast<cudaStream_t>(stream));
   return chunk_fwd_launch(*a, ws, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -134,6 +143,7 @@ int gdn2_chunk_bwd(const gdn2_chunk_args* a, const gdn2_chunk_grads* gr, const v
   chunk_ws_layout(*a, const_cast<void*>(workspace), &ws);
   BwdWs bw;
   bwd_ws_layout(*a, bwd_workspace, &bw);
+  if (a->dtype_qkv == GDN2_F32) return chunk_bwd_fp32_launch(*a, *gr, ws, bw, reinterpret_cast<cudaStream_t>(stream));
   return chunk_bwd_launch(*a, *gr, ws, bw, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -22,12 +22,22 @@ struct ChunkWs {
   __nv_bfloat16* h;    // per-chunk entering state, transposed: [NT, H, V, K]
   float* segX;         // segmented scan: segment states [N*H, nseg, K, V] fp32 (or nullptr)
   float* segM;         // segmented scan: segment transitions [N*H, nseg, K, K] fp32 (kept for the backward)
+  // fp32 inputs (dtype_qkv == GDN2_F32) run the token-serial fp32 path instead:
+  float* qf;           // l2-normalised q, fp32 [tokens, H, K] (with l2norm; else aliases q)
+  float* kf;
+  float* gf;           // activated log-decay, fp32 [tokens, H, K] (with the gate in the kernel; else aliases g)
+  float* ckpt;         // state entering each chunk, fp32 [NT, H, K, V] (saved for the backward)
 };
 
 struct BwdWs {
   __nv_bfloat16* dh;   // state cotangent at the end of each chunk, transposed [NT, H, V, K]
   __nv_bfloat16* dvn;  // cotangent of v_new [tokens, H, V]
   float* segZ;         // segmented reverse scan: segment state cotangents [N*H, nseg, K, V] fp32
+  // fp32 path:
+  float* tok_states;   // the states entering each token of one chunk, fp32 [N*H, 64, K, V]
+  float* dqf;          // cotangents of the normalised q, k and the activated gate, fp32 [tokens, H, K]
+  float* dkf;          //   (with l2norm / the gate; else the outputs are written directly)
+  float* dgf;
 };
 
 inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
@@ -89,6 +99,19 @@ inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws)
     return base ? (void*)((char*)base + o) : nullptr;
   };
   ChunkWs w{};
+  if (a.dtype_qkv == GDN2_F32) {
+    const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
+    w.qf = l2 ? (float*)take(tok * H * K * 4) : (float*)a.q;
+    w.kf = l2 ? (float*)take(tok * H * K * 4) : (float*)a.k;
+    if (l2) {
+      w.q_rstd = (float*)take(tok * H * 4);
+      w.k_rstd = (float*)take(tok * H * 4);
+    }
+    w.gf = gate ? (float*)take(tok * H * K * 4) : (float*)a.g;
+    if (save) w.ckpt = (float*)take((size_t)a.NT * H * K * V * 4);
+    if (ws) *ws = w;
+    return off;
+  }
   w.G = (float*)take(tok * H * K * 4);
   w.Aqk = (__nv_bfloat16*)take(tok * H * 64 * 2);
   w.Akk = (__nv_bfloat16*)take(tok * H * 64 * 2);
@@ -130,6 +153,16 @@ inline size_t bwd_ws_layout(const gdn2_chunk_args& a, void* base, BwdWs* ws) {
     return base ? (void*)((char*)base + o) : nullptr;
   };
   BwdWs w{};
+  if (a.dtype_qkv == GDN2_F32) {
+    w.tok_states = (float*)take((size_t)a.N * H * 64 * K * V * 4);
+    if (a.flags & GDN2_L2NORM_QK) {
+      w.dqf = (float*)take(tok * H * K * 4);
+      w.dkf = (float*)take(tok * H * K * 4);
+    }
+    if (a.flags & GDN2_GATE_IN_KERNEL) w.dgf = (float*)take(tok * H * K * 4);
+    if (ws) *ws = w;
+    return off;
+  }
   w.dh = (__nv_bfloat16*)take((size_t)a.NT * H * K * V * 2);
   w.dvn = (__nv_bfloat16*)take(tok * H * V * 2);
   const SegPlan plan = seg_plan(a);
@@ -142,10 +175,22 @@ inline size_t bwd_ws_layout(const gdn2_chunk_args& a, void* base, BwdWs* ws) {
 GDN2_DEV constexpr int anchor_row0(int i) { return 8 * i * (i + 1); }
 
 int chunk_fwd_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
+// fp32 inputs: token-serial fp32 forward / backward (chunk_fp32.cu)
+int chunk_fwd_fp32_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s);
+int chunk_bwd_fp32_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
+                          cudaStream_t s);
 int chunk_transition_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s);
 int chunk_bwd_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const ChunkWs& ws, const BwdWs& bw,
                      cudaStream_t s);
-int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s);
+// Checkpoints of the token-serial kernel for the chunked fp32 path: the fp32
+// state entering every 64-token chunk, [NT, H, K, V] (global chunk index from
+// chunk_offset for varlen, n * chunks_per_seq + c for dense batches).
+struct RecCheckpoints {
+  float* states = nullptr;
+  const int32_t* chunk_offset = nullptr;
+  int64_t chunks_per_seq = 0;
+};
+int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s, const RecCheckpoints& ck = RecCheckpoints{});
 
 // tcgen05 forward scan (scan_tc.cu), d_k = d_v = 128
 bool scan_fwd_tc_supported(const gdn2_chunk_args& a);

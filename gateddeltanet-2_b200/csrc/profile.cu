@@ -16,7 +16,8 @@ const char* kNames[kNumKernels] = {"chunk_intra_kernel", "chunk_scan_fwd_kernel"
                                    "chunk_bwd_intra_kernel", "recurrent_kernel", "cp_kernel",
                                    "chunk_scan_fwd_tc_kernel", "chunk_scan_bwd_tc_kernel",
                                    "layer_prep_fwd_kernel", "layer_prep_bwd_kernel",
-                                   "norm_gate_fwd_kernel", "norm_gate_bwd_kernel", "seg_fold_kernel"};
+                                   "norm_gate_fwd_kernel", "norm_gate_bwd_kernel", "seg_fold_kernel",
+                                   "chunk_bwd_fp32_kernel", "fp32_prep_epilogue_kernel"};
 
 struct Pending {
   int id;

@@ -4,7 +4,7 @@
 
 namespace gdn2 {
 enum KernelId { kKIntra = 0, kKScanFwd, kKScanBwd, kKBwdIntra, kKRecurrent, kKCp, kKScanFwdTc, kKScanBwdTc,
-                kKLayerPrepFwd, kKLayerPrepBwd, kKNormGateFwd, kKNormGateBwd, kKSegFold, kNumKernels };
+                kKLayerPrepFwd, kKLayerPrepBwd, kKNormGateFwd, kKNormGateBwd, kKSegFold, kKBwdFp32, kKFp32Aux, kNumKernels };
 bool prof_on();
 void prof_begin(int id, cudaStream_t s);
 void prof_end(int id, cudaStream_t s);

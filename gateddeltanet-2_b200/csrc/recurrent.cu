@@ -9,6 +9,9 @@
 // once with 128-bit stores.  Both K-reductions (S^T(b*k) and S^T q) come out
 // of the same pass over the tile: warp shuffles, then a cross-warp smem step.
 // o uses S_new^T q = S_dec^T q + u (k.q), so the state is touched once per token.
+#include <type_traits>
+
+#include "chunk_layout.cuh"
 #include "common.cuh"
 #include "profile.cuh"
 
@@ -24,9 +27,9 @@ constexpr int kRecRowStep = kRecThreads / kRecColGroups;  // 16 rows per pass
 // 8 resident CTAs per SM (64 registers a thread): the 16 KiB state tiles of
 // eight CTAs in flight per SM keep the HBM pipe full (measured 83% of the copy
 // bandwidth at 256 x 16 heads, against 66% at the unconstrained 127 registers).
-template <typename TQ, typename TG, int K, bool kTransposed>
+template <typename TQ, typename TG, int K, bool kTransposed, bool kCkpt>
 __global__ void __launch_bounds__(kRecThreads, 8)
-recurrent_kernel(gdn2_recurrent_args a) {
+recurrent_kernel(gdn2_recurrent_args a, RecCheckpoints ck) {
   constexpr int kRows = K / kRecRowStep;  // rows per thread (8 for K=128)
   __shared__ float s_q[K], s_k[K], s_bk[K], s_alpha[K];
   __shared__ float s_v[kRecBV], s_w[kRecBV];
@@ -99,6 +102,15 @@ recurrent_kernel(gdn2_recurrent_args a) {
 
   for (int64_t t = 0; t < T; ++t) {
     const int64_t tok = bos + t;
+    // the chunked fp32 path keeps the state entering every 64-token chunk
+    if (kCkpt && (t & 63) == 0) {
+      const int64_t c = (ck.chunk_offset ? (int64_t)ck.chunk_offset[n] : n * ck.chunks_per_seq) + (t >> 6);
+      float* dst = ck.states + (c * HV + hv) * (int64_t)K * V;
+#pragma unroll
+      for (int i = 0; i < kRows; ++i)
+        *reinterpret_cast<float4*>(dst + (int64_t)(r0 + i * kRecRowStep) * V + c0) =
+            make_float4(st[i][0], st[i][1], st[i][2], st[i][3]);
+    }
     // ---- per-token vectors into smem, with l2norm / gate activation ----------
     float pq = 0.f, pk = 0.f, pqk = 0.f;
     for (int c = tid; c < K; c += kRecThreads) {
@@ -242,32 +254,39 @@ recurrent_kernel(gdn2_recurrent_args a) {
 }
 
 template <typename TQ, typename TG, int K>
-cudaError_t launch_rec(const gdn2_recurrent_args& a, cudaStream_t s) {
+cudaError_t launch_rec(const gdn2_recurrent_args& a, const RecCheckpoints& ck, cudaStream_t s) {
   const int64_t grid = a.N * a.HV * (a.V / kRecBV);
   if (grid == 0) return cudaSuccess;
   ProfScope ps(kKRecurrent, s);
-  if (a.flags & GDN2_TRANSPOSE_STATE)
-    recurrent_kernel<TQ, TG, K, true><<<(unsigned)grid, kRecThreads, 0, s>>>(a);
-  else
-    recurrent_kernel<TQ, TG, K, false><<<(unsigned)grid, kRecThreads, 0, s>>>(a);
+  const bool tr = a.flags & GDN2_TRANSPOSE_STATE;
+  if (ck.states) {  // the chunked fp32 path (fp32 inputs only)
+    if constexpr (std::is_same<TQ, float>::value && std::is_same<TG, float>::value) {
+      if (tr) recurrent_kernel<TQ, TG, K, true, true><<<(unsigned)grid, kRecThreads, 0, s>>>(a, ck);
+      else recurrent_kernel<TQ, TG, K, false, true><<<(unsigned)grid, kRecThreads, 0, s>>>(a, ck);
+      return cudaGetLastError();
+    }
+    return cudaErrorInvalidValue;
+  }
+  if (tr) recurrent_kernel<TQ, TG, K, true, false><<<(unsigned)grid, kRecThreads, 0, s>>>(a, ck);
+  else recurrent_kernel<TQ, TG, K, false, false><<<(unsigned)grid, kRecThreads, 0, s>>>(a, ck);
   return cudaGetLastError();
 }
 
 template <typename TQ, typename TG>
-cudaError_t dispatch_k(const gdn2_recurrent_args& a, cudaStream_t s) {
-  if (a.K == 128) return launch_rec<TQ, TG, 128>(a, s);
-  return launch_rec<TQ, TG, 64>(a, s);
+cudaError_t dispatch_k(const gdn2_recurrent_args& a, const RecCheckpoints& ck, cudaStream_t s) {
+  if (a.K == 128) return launch_rec<TQ, TG, 128>(a, ck, s);
+  return launch_rec<TQ, TG, 64>(a, ck, s);
 }
 
 }  // namespace
 
-int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s) {
+int recurrent_fwd(const gdn2_recurrent_args& a, cudaStream_t s, const RecCheckpoints& ck) {
   cudaError_t e;
   const bool qbf = a.dtype_qkv == GDN2_BF16, gbf = a.dtype_gbw == GDN2_BF16;
-  if (qbf && gbf) e = dispatch_k<__nv_bfloat16, __nv_bfloat16>(a, s);
-  else if (qbf) e = dispatch_k<__nv_bfloat16, float>(a, s);
-  else if (gbf) e = dispatch_k<float, __nv_bfloat16>(a, s);
-  else e = dispatch_k<float, float>(a, s);
+  if (qbf && gbf) e = dispatch_k<__nv_bfloat16, __nv_bfloat16>(a, ck, s);
+  else if (qbf) e = dispatch_k<__nv_bfloat16, float>(a, ck, s);
+  else if (gbf) e = dispatch_k<float, __nv_bfloat16>(a, ck, s);
+  else e = dispatch_k<float, float>(a, ck, s);
   return e == cudaSuccess ? 0 : -static_cast<int>(e);
 }
 

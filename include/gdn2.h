@@ -101,7 +101,9 @@ typedef struct gdn2_chunk_args {
   float scale;           /* attention scale (reference default K^-0.5) */
   float lower_bound;     /* used with GDN2_LOWER_BOUND */
   int32_t flags;         /* enum gdn2_flags */
-  int32_t dtype_qkv;     /* q, k, v, do and o: GDN2_BF16 */
+  int32_t dtype_qkv;     /* q, k, v, do and o (and dq, dk, dv): GDN2_BF16, or GDN2_F32 for the
+                            fp32 path (every input fp32: dtype_bw GDN2_F32, no GDN2_G_BF16),
+                            which computes the recurrence token by token in fp32 */
   int32_t dtype_bw;      /* b, w (and db, dw): GDN2_BF16 or GDN2_F32 */
   const void* q;
   const void* k;
@@ -139,8 +141,9 @@ size_t gdn2_chunk_bwd_workspace_size(const gdn2_chunk_args* a);
 
 /* Buffers of the forward workspace a caller may read after gdn2_chunk_fwd. */
 enum gdn2_ws_buffer {
-  GDN2_WS_CHUNK_STATES = 0 /* per-chunk entering states h, bf16, transposed [NT, H, V, K];
-                              present with GDN2_SAVE_FOR_BWD */
+  GDN2_WS_CHUNK_STATES = 0 /* per-chunk entering states h, present with GDN2_SAVE_FOR_BWD:
+                              bf16 transposed [NT, H, V, K] (bf16 inputs), or fp32 [NT, H, K, V]
+                              (GDN2_F32 inputs) */
 };
 /* Byte offset of buffer `which` inside the workspace gdn2_chunk_fwd fills for
  * these arguments, or (size_t)-1 when these arguments keep no such buffer

@@ -69,7 +69,8 @@ def test_segmented_scan_workspace(gdn2):
 
 
 @pytest.mark.parametrize("kw,code", [
-    (dict(K=96), 4), (dict(V=32), 4), (dict(dtype_qkv=1), 3), (dict(NT=255), 2),
+    (dict(K=96), 4), (dict(V=32), 4), (dict(dtype_qkv=1, dtype_bw=0), 3), (dict(dtype_qkv=2), 3),
+    (dict(dtype_qkv=1, flags=1 << 9), 7), (dict(NT=255), 2),
     (dict(N=3), 2), (dict(flags=4), 7),
 ])
 def test_invalid_chunk_args_rejected(gdn2, kw, code):

@@ -50,27 +50,50 @@ def _run_case(gdn2, name, backward=True):
     return meta, t, o, ht, leaves
 
 
+# fp32 inputs take the fp32 path (the recurrence in fp32, like the reference's
+# fp32 path, which is within ~5e-7 of the naive fp32 recurrence): those cases
+# are held to 1e-4 absolute + 1e-4 relative instead of the bf16 bound.
+FP32_TOL = dict(rtol=1e-4, atol=1e-4)
+
+
+def _tol(meta):
+    return FP32_TOL if meta["qkv_dtype"] == "float32" else {}
+
+
 @pytest.mark.parametrize("name", case_names("chunk"))
 def test_chunk_forward_matches_reference_golden(gdn2, name):
-    _, t, o, ht, _ = _run_case(gdn2, name, backward=False)
-    assert_close(o, t["out_o"], "o")
-    assert_close(ht, t["out_ht"], "ht")
+    meta, t, o, ht, _ = _run_case(gdn2, name, backward=False)
+    assert_close(o, t["out_o"], "o", **_tol(meta))
+    assert_close(ht, t["out_ht"], "ht", **_tol(meta))
 
 
 @pytest.mark.parametrize("name", case_names("chunk"))
 def test_chunk_backward_matches_reference_golden(gdn2, name):
     meta, t, o, ht, leaves = _run_case(gdn2, name, backward=True)
-    assert_close(o, t["out_o"], "o")
-    assert_close(ht, t["out_ht"], "ht")
+    tol = _tol(meta)
+    assert_close(o, t["out_o"], "o", **tol)
+    assert_close(ht, t["out_ht"], "ht", **tol)
     masses = {}
     if meta["gate"]:
         mA, mdt = gate_param_masses(t["in_g"], t["in_dt_bias"], t["grad_g"], meta["H"])
         masses = {"A_log": mA, "dt_bias": mdt}
     for n, leaf in leaves.items():
         if n in masses:
-            assert_close_reduced(leaf.grad, t[f"grad_{n}"], masses[n], f"d{n}", rtol=RTOL_SUM)
+            assert_close_reduced(leaf.grad, t[f"grad_{n}"], masses[n], f"d{n}",
+                                 rtol=tol.get("rtol", RTOL_SUM))
         else:
-            assert_close(leaf.grad, t[f"grad_{n}"], f"d{n}")
+            assert_close(leaf.grad, t[f"grad_{n}"], f"d{n}", **tol)
+
+
+def test_config1_fp32_matches_reference_golden_at_fp32_bound(gdn2):
+    """BASELINE config 1 exactly (fp32, B=1, H=2, T=256, d=64, chunk 64): the
+    reference's own chunk op output and all six gradients to 1e-4."""
+    meta, t, o, ht, leaves = _run_case(gdn2, "chunk_c1_fp32", backward=True)
+    assert (meta["B"], meta["H"], meta["T"], meta["K"], meta["V"]) == (1, 2, 256, 64, 64)
+    assert o.dtype == torch.float32
+    assert_close(o, t["out_o"], "o", **FP32_TOL)
+    for n in "qkvgbw":
+        assert_close(leaves[n].grad, t[f"grad_{n}"], f"d{n}", **FP32_TOL)
 
 
 def _inputs(seed, B, T, H, K, V, gate_scale=0.1, bw=torch.float32):
@@ -239,6 +262,92 @@ def test_intermediate_states_match_oracle_prefix_states(gdn2, K, V, transpose):
         if transpose:
             got = got.swapaxes(-1, -2)
         np.testing.assert_allclose(got, ref, rtol=2e-3 + 2 ** -8, atol=1e-2, err_msg=f"h[{c}]")
+
+
+@pytest.mark.parametrize("K,V,gate,l2", [(128, 128, True, True), (64, 128, False, False),
+                                         (128, 64, False, True), (64, 64, True, False)])
+def test_fp32_path_matches_oracle_at_fp32_bound(gdn2, K, V, gate, l2):
+    """fp32 inputs: forward, final state and every gradient (with h0, dht,
+    the gate and l2norm in the kernel) against the fp64 oracle to 1e-4."""
+    B, T, H = 2, 150, 2
+    g = torch.Generator().manual_seed(K + V + gate)
+    q = torch.randn(B, T, H, K, generator=g) * (3.0 if l2 else 1.0)
+    k = torch.randn(B, T, H, K, generator=g)
+    if not l2:
+        q, k = (torch.nn.functional.normalize(x, dim=-1) for x in (q, k))
+    v = torch.randn(B, T, H, V, generator=g)
+    graw = torch.randn(B, T, H, K, generator=g) if gate else -torch.nn.functional.softplus(
+        torch.randn(B, T, H, K, generator=g)) * 0.1
+    b = torch.sigmoid(torch.randn(B, T, H, K, generator=g))
+    w = torch.sigmoid(torch.randn(B, T, H, V, generator=g))
+    h0 = torch.randn(B, H, K, V, generator=g) * 0.1
+    do = torch.randn(B, T, H, V, generator=g)
+    dht = torch.randn(B, H, K, V, generator=g) * 0.1
+    A_log = torch.rand(H, generator=g) * 2.0
+    dt_bias = torch.randn(H * K, generator=g) * 0.5
+    leaves = [x.cuda().requires_grad_(True) for x in (q, k, v, graw, b, w)]
+    h0_d = h0.cuda().requires_grad_(True)
+    kw = {}
+    if gate:
+        A_d, dt_d = A_log.cuda().requires_grad_(True), dt_bias.cuda().requires_grad_(True)
+        kw = dict(A_log=A_d, dt_bias=dt_d)
+    o, ht = gdn2.chunk_gdn2(*leaves, initial_state=h0_d, output_final_state=True,
+                            use_qk_l2norm_in_kernel=l2, use_gate_in_kernel=gate, **kw)
+    assert o.dtype == torch.float32
+    torch.autograd.backward([o, ht], [do.cuda(), dht.cuda()])
+    torch.cuda.synchronize()
+    r = orc.chunk_gdn2(*(x.double().numpy() for x in (q, k, v, graw, b, w)), initial_state=h0.double().numpy(),
+                       output_final_state=True, use_qk_l2norm_in_kernel=l2, use_gate_in_kernel=gate,
+                       A_log=A_log.double().numpy() if gate else None,
+                       dt_bias=dt_bias.double().numpy() if gate else None,
+                       do=do.double().numpy(), dht=dht.double().numpy())
+    assert_close(o, r.o, "o", **FP32_TOL)
+    assert_close(ht, r.final_state, "ht", **FP32_TOL)
+    for n, leaf in zip("qkvgbw", leaves):
+        assert_close(leaf.grad, r.grads[n], f"d{n}", **FP32_TOL)
+    assert_close(h0_d.grad, r.grads["h0"], "dh0", **FP32_TOL)
+    if gate:
+        mA, mdt = gate_param_masses(graw, dt_bias, r.grads["g"], H)
+        assert_close_reduced(A_d.grad, r.grads["A_log"], mA, "dA_log", rtol=1e-5, atol=1e-4)
+        assert_close_reduced(dt_d.grad, r.grads["dt_bias"], mdt, "ddt_bias", rtol=1e-5, atol=1e-4)
+
+
+def test_fp32_intermediate_states_and_varlen(gdn2):
+    """fp32 chunk states (return_intermediate_states, kept in fp32) and a
+    packed batch with a transposed state layout on the fp32 path."""
+    cu = [0, 70, 71, 200]
+    T, H, K, V = cu[-1], 2, 64, 128
+    g = torch.Generator().manual_seed(12)
+    q, k = (torch.nn.functional.normalize(torch.randn(1, T, H, K, generator=g), dim=-1) for _ in range(2))
+    v = torch.randn(1, T, H, V, generator=g)
+    gg = -torch.nn.functional.softplus(torch.randn(1, T, H, K, generator=g)) * 0.1
+    b = torch.sigmoid(torch.randn(1, T, H, K, generator=g))
+    w = torch.sigmoid(torch.randn(1, T, H, V, generator=g))
+    h0 = torch.randn(3, H, K, V, generator=g) * 0.1
+    with torch.inference_mode():
+        o, htT, hs = gdn2.chunk_gdn2(*(x.cuda() for x in (q, k, v, gg, b, w)),
+                                     initial_state=h0.transpose(-1, -2).contiguous().cuda(),
+                                     output_final_state=True, cu_seqlens=torch.tensor(cu, device="cuda"),
+                                     return_intermediate_states=True, transpose_state_layout=True)
+    torch.cuda.synchronize()
+    assert hs.dtype == torch.float32 and hs.shape == (1, 6, H, V, K)
+    r = orc.chunk_gdn2(*(x.double().numpy() for x in (q, k, v, gg, b, w)), initial_state=h0.double().numpy(),
+                       output_final_state=True, cu_seqlens=cu)
+    assert_close(o, r.o, "o", **FP32_TOL)
+    assert_close(htT.transpose(-1, -2), r.final_state, "ht", **FP32_TOL)
+    x = [t.double().numpy() for t in (q, k, v, gg, b, w)]
+    # chunk c enters after the tokens [bos, t_end) of its sequence: seq 0 (70 tokens) has
+    # chunks 0, 1; seq 1 (1 token) chunk 2; seq 2 (129 tokens) chunks 3, 4, 5
+    starts = {0: (0, 0), 1: (0, 64), 2: (1, 70), 3: (2, 71), 4: (2, 135), 5: (2, 199)}
+    for c, (n, t_end) in starts.items():
+        bos = cu[n]
+        if t_end == bos:
+            ref = h0.double().numpy()[n]
+        else:
+            _, ref, _ = orc.recurrent_fwd(*(t[:, bos:t_end] for t in x), K ** -0.5, h0.double().numpy()[n:n + 1])
+            ref = ref[0]
+        np.testing.assert_allclose(hs[0, c].transpose(-1, -2).double().cpu().numpy(), ref, rtol=1e-4, atol=1e-4,
+                                   err_msg=f"h[{c}]")
 
 
 # Segmented scans (few (sequence, head) pairs, at least 32 chunks per sequence):
