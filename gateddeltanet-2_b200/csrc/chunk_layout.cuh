@@ -22,6 +22,7 @@ struct ChunkWs {
   __nv_bfloat16* h;    // per-chunk entering state, transposed: [NT, H, V, K]
   float* segX;         // segmented scan: segment states [N*H, nseg, K, V] fp32 (or nullptr)
   float* segM;         // segmented scan: segment transitions [N*H, nseg, K, K] fp32 (kept for the backward)
+  float* segP;         // segmented CP transition: products of the segment transitions [N*H, nseg, K, K]
   // fp32 inputs (dtype_qkv == GDN2_F32) run the token-serial fp32 path instead:
   float* qf;           // l2-normalised q, fp32 [tokens, H, K] (with l2norm; else aliases q)
   float* kf;
@@ -86,6 +87,33 @@ inline SegPlan seg_plan(const gdn2_chunk_args& a) {
   return best < 0.85 * base ? cand : p;
 }
 
+// The context-parallel transition of a shard ([M | h_e], gdn2_cp_transition)
+// in segments: one pass computes every segment's M_s and h_s (two CTAs per
+// segment), two folds compose them (no second pass).  Same cost model.
+inline SegPlan trans_plan(const gdn2_chunk_args& a) {
+  const int64_t nts = (a.T + 63) / 64;
+  SegPlan p{1, (int)nts};
+  if (a.K != 128 || a.V != 128 || a.cu_seqlens || a.N <= 0 || nts < kSegMinChunks) return p;
+  const int64_t NH = a.N * a.H;
+  auto waves = [](int64_t ctas) { return (double)((ctas + kPlanSms - 1) / kPlanSms); };
+  constexpr double kStep = 3.3, kPass = 8.0, kFoldStep = 2.0, kFoldLaunch = 5.0;
+  const double base = waves(2 * NH) * (double)nts * kStep + kPass;
+  double best = base;
+  SegPlan cand = p;
+  for (int64_t n = 2; n <= 64; ++n) {
+    const int64_t L = (nts + n - 1) / n;
+    const int64_t nn = (nts + L - 1) / L;
+    if (nn < 2 || L < 2) continue;
+    const double cost = waves(2 * NH * nn) * (double)L * kStep + kPass +
+                        2 * (waves(NH * kFoldCtasPerPair) * (double)(nn - 1) * kFoldStep + kFoldLaunch);
+    if (cost < best) {
+      best = cost;
+      cand = SegPlan{(int)nn, (int)L};
+    }
+  }
+  return best < 0.85 * base ? cand : p;
+}
+
 // Carves `base` (or computes the size when base == nullptr).
 inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws) {
   const size_t tok = (size_t)a.B * (size_t)a.T;
@@ -133,11 +161,13 @@ inline size_t chunk_ws_layout(const gdn2_chunk_args& a, void* base, ChunkWs* ws)
     w.qn = (__nv_bfloat16*)a.q;
     w.kn = (__nv_bfloat16*)a.k;
   }
-  const SegPlan plan = seg_plan(a);
-  if (plan.nseg > 1) {
-    const size_t nsl = (size_t)a.N * H * (size_t)plan.nseg;
+  const SegPlan plan = seg_plan(a), tplan = trans_plan(a);
+  const int nbuf = plan.nseg > tplan.nseg ? plan.nseg : tplan.nseg;
+  if (nbuf > 1) {
+    const size_t nsl = (size_t)a.N * H * (size_t)nbuf;
     w.segX = (float*)take(nsl * K * V * 4);
     w.segM = (float*)take(nsl * K * K * 4);
+    if (tplan.nseg > 1) w.segP = (float*)take(nsl * K * K * 4);
   }
   if (ws) *ws = w;
   return off;

@@ -124,9 +124,11 @@ GDN2_DEV void copy_rows_out(const __nv_bfloat16 (*tile)[64 * 64], __nv_bfloat16*
 struct SegArgs {
   int nseg;      // segments per sequence
   int seg_len;   // chunks per segment
-  int pass;      // 0: the whole sequence per CTA; 1, 2: the passes above; 3: CP transition
+  int pass;      // 0: the whole sequence per CTA; 1, 2: the passes above; 3: CP transition;
+                 // 4: CP transition in segments (every segment's M_s and h_s)
   float* X;      // [N*H, nseg, K, V] segment states (the reverse scan: cotangents)
   const float* M;  // [N*H, nseg, K, K] segment transitions
+  float* P = nullptr;  // pass 4: [N*H, nseg, K, K], segment 0's transition goes to P[0]
 };
 
 enum ScanMode { kModeFull = 0, kModeTransM = 1, kModeTransH = 2 };
@@ -177,6 +179,21 @@ GDN2_DEV ScanJob fwd_job(const gdn2_chunk_args& a, const SegArgs& sg, int64_t nh
   }
   float* X = sg.X + nh * sg.nseg * kKV;
   int seg;
+  if (sg.pass == 4) {
+    seg = y / 2;
+    if (y & 1) {
+      j.mode = kModeTransH;
+      j.init = seg == 0 ? h0 : nullptr;
+      j.exit = X + seg * kKV;
+    } else {
+      j.mode = kModeTransM;
+      j.identity = true;
+      j.exit = seg == 0 ? sg.P + nh * sg.nseg * kKV : const_cast<float*>(sg.M) + (nh * sg.nseg + seg) * kKV;
+    }
+    j.cb = seg * sg.seg_len;
+    j.ce = min(j.cb + sg.seg_len, nchunks);
+    return j;
+  }
   if (sg.pass == 1) {
     if (y == 0) {
       seg = 0;
@@ -944,9 +961,13 @@ GDN2_DEV void fold_cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(tc::smem_u32(dst)), "l"(src));
 }
 
-template <bool kBwd>
+// nsteps folds (steps 1 .. nsteps) over buffers of nseg segments; without
+// kAdd the addend is zero (X[s] <- M_s X[s-1]).  With `out` the last result is
+// also written to out[nh] (rows of out_ld floats, from column out_col).
+template <bool kBwd, bool kAdd>
 __global__ void __launch_bounds__(kFoldThreads)
-seg_fold_kernel(const float* __restrict__ M, float* __restrict__ X, int nseg) {
+seg_fold_kernel(const float* __restrict__ M, float* __restrict__ X, int nseg, int nsteps, float* out, int out_ld,
+                int out_col) {
   extern __shared__ __align__(16) float fold_smem[];
   float* const Mb0 = fold_smem;
   float* const Mb1 = fold_smem + kTcK * kFoldLd;
@@ -967,20 +988,22 @@ seg_fold_kernel(const float* __restrict__ M, float* __restrict__ X, int nseg) {
     }
     asm volatile("cp.async.commit_group;\n" ::);
   };
-  if (nseg < 3) return;
+  if (nsteps < 1) return;
   load_m(1, Mb1);
   float4 add0 = make_float4(0.f, 0.f, 0.f, 0.f), add1 = add0;  // the next addend (half 0)
   if (hf == 0) {
     const float4* s4 = reinterpret_cast<const float4*>(row_of(0));
     *reinterpret_cast<float4*>(&Ss[r][0]) = s4[0];
     *reinterpret_cast<float4*>(&Ss[r][4]) = s4[1];
-    const float4* a4 = reinterpret_cast<const float4*>(row_of(1));
-    add0 = a4[0];
-    add1 = a4[1];
+    if (kAdd) {
+      const float4* a4 = reinterpret_cast<const float4*>(row_of(1));
+      add0 = a4[0];
+      add1 = a4[1];
+    }
   }
-  for (int step = 1; step <= nseg - 2; ++step) {
+  for (int step = 1; step <= nsteps; ++step) {
     const float* Ms = (step & 1) ? Mb1 : Mb0;
-    if (step + 1 <= nseg - 2) {
+    if (step + 1 <= nsteps) {
       load_m(step + 1, (step & 1) ? Mb0 : Mb1);
       asm volatile("cp.async.wait_group 1;\n" ::);
     } else {
@@ -990,7 +1013,7 @@ seg_fold_kernel(const float* __restrict__ M, float* __restrict__ X, int nseg) {
     float acc[kFoldBV];
     acc[0] = add0.x, acc[1] = add0.y, acc[2] = add0.z, acc[3] = add0.w;
     acc[4] = add1.x, acc[5] = add1.y, acc[6] = add1.z, acc[7] = add1.w;
-    if (hf == 0 && step + 1 <= nseg - 2) {  // the next step's addend, in flight during this one
+    if (kAdd && hf == 0 && step + 1 <= nsteps) {  // the next step's addend, in flight during this one
       const float4* a4 = reinterpret_cast<const float4*>(row_of(step + 1));
       add0 = a4[0];
       add1 = a4[1];
@@ -1035,6 +1058,11 @@ seg_fold_kernel(const float* __restrict__ M, float* __restrict__ X, int nseg) {
       float4* xp = reinterpret_cast<float4*>(row_of(step));
       xp[0] = o0;
       xp[1] = o1;
+      if (out && step == nsteps) {
+        float4* op = reinterpret_cast<float4*>(out + (nh * kTcK + r) * (int64_t)out_ld + out_col + v0);
+        op[0] = o0;
+        op[1] = o1;
+      }
     }
   }
 }
@@ -1083,12 +1111,13 @@ bool scan_fwd_tc_supported(const gdn2_chunk_args& a) { return a.K == kTcK && a.V
 
 namespace {
 
-int launch_fold(bool bwd, const float* M, float* X, int nseg, int64_t NH, cudaStream_t s) {
-  if (nseg < 3) return 0;
-  auto k = bwd ? seg_fold_kernel<true> : seg_fold_kernel<false>;
+int launch_fold(bool bwd, bool add, const float* M, float* X, int nseg, int nsteps, int64_t NH, cudaStream_t s,
+                float* out = nullptr, int out_ld = 0, int out_col = 0) {
+  if (nsteps < 1) return 0;
+  auto k = bwd ? seg_fold_kernel<true, true> : (add ? seg_fold_kernel<false, true> : seg_fold_kernel<false, false>);
   GDN2_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kFoldSmem));
   ProfScope ps(kKSegFold, s);
-  k<<<dim3(kTcV / kFoldBV, (unsigned)NH), kFoldThreads, kFoldSmem, s>>>(M, X, nseg);
+  k<<<dim3(kTcV / kFoldBV, (unsigned)NH), kFoldThreads, kFoldSmem, s>>>(M, X, nseg, nsteps, out, out_ld, out_col);
   GDN2_LAUNCH_CHECK();
   return 0;
 }
@@ -1097,7 +1126,8 @@ int launch_fold(bool bwd, const float* M, float* X, int nseg, int64_t NH, cudaSt
 int fwd_tc_pass(const gdn2_chunk_args& a, const ChunkWs& ws, const SegArgs& sg, float* maps, unsigned grid_y,
                 cudaStream_t s) {
   const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T, H = (uint64_t)a.H;
-  const bool save = (a.flags & GDN2_SAVE_FOR_BWD) && sg.pass != 3;
+  const bool trans = sg.pass == 3 || sg.pass == 4;  // the CP transition writes no outputs
+  const bool save = (a.flags & GDN2_SAVE_FOR_BWD) && !trans;
   auto kern = save ? chunk_scan_fwd_tc_kernel<true> : chunk_scan_fwd_tc_kernel<false>;
   const int smem = (int)sizeof(TcSmem) + 1024;
   // a runtime call first: it binds this thread's context, which the driver's
@@ -1109,7 +1139,7 @@ int fwd_tc_pass(const gdn2_chunk_args& a, const ChunkWs& ws, const SegArgs& sg, 
       !token_map(&mA, ws.Aqk, kChunk, H, tokens))
     return GDN2_ERR_TENSOR_MAP;
   // the transition writes no o: its output maps are never used
-  if (sg.pass == 3) mO = mY;
+  if (trans) mO = mY;
   else if (!token_map(&mO, a.o, kTcV, H, tokens)) return GDN2_ERR_TENSOR_MAP;
   if (save ? !token_map(&mVN, ws.v_new, kTcV, H, tokens) ||
                  !rows_map(&mH, ws.h, kTcK, (uint64_t)a.NT * H * kTcV)
@@ -1150,7 +1180,7 @@ int scan_fwd_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t
   const int n = plan.nseg;
   int st = fwd_tc_pass(a, ws, SegArgs{n, plan.seg_len, 1, ws.segX, ws.segM}, nullptr, (unsigned)(2 * n - 3), s);
   if (st) return st;
-  if ((st = launch_fold(false, ws.segM, ws.segX, n, a.N * a.H, s))) return st;
+  if ((st = launch_fold(false, true, ws.segM, ws.segX, n, n - 2, a.N * a.H, s))) return st;
   return fwd_tc_pass(a, ws, SegArgs{n, plan.seg_len, 2, ws.segX, ws.segM}, nullptr, (unsigned)(n - 1), s);
 }
 
@@ -1161,13 +1191,23 @@ int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, cons
   const int n = plan.nseg;
   int st = bwd_tc_pass(a, g, ws, bw, SegArgs{n, plan.seg_len, 1, bw.segZ, ws.segM}, (unsigned)(n - 1), s);
   if (st) return st;
-  if ((st = launch_fold(true, ws.segM, bw.segZ, n, a.N * a.H, s))) return st;
+  if ((st = launch_fold(true, true, ws.segM, bw.segZ, n, n - 2, a.N * a.H, s))) return st;
   return bwd_tc_pass(a, g, ws, bw, SegArgs{n, plan.seg_len, 2, bw.segZ, ws.segM}, (unsigned)(n - 1), s);
 }
 
 int scan_trans_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s) {
-  const SegPlan plan = seg_plan(a);
-  return fwd_tc_pass(a, ws, SegArgs{1, plan.seg_len, 3, nullptr, nullptr}, maps, 2, s);
+  const SegPlan plan = trans_plan(a);
+  if (plan.nseg <= 1) return fwd_tc_pass(a, ws, SegArgs{1, plan.seg_len, 3, nullptr, nullptr}, maps, 2, s);
+  // every segment's M_s (segment 0's into P[0]) and h_s (segment 0's from the
+  // shard's initial state), then h_e = fold of the h_s and M = P[n-1] = M_{n-1} .. M_0
+  const int n = plan.nseg;
+  SegArgs sg{n, plan.seg_len, 4, ws.segX, ws.segM};
+  sg.P = ws.segP;
+  int st = fwd_tc_pass(a, ws, sg, maps, (unsigned)(2 * n), s);
+  if (st) return st;
+  const int ld = kTcK + kTcV;
+  if ((st = launch_fold(false, true, ws.segM, ws.segX, n, n - 1, a.N * a.H, s, maps, ld, kTcK))) return st;
+  return launch_fold(false, false, ws.segM, ws.segP, n, n - 1, a.N * a.H, s, maps, ld, 0);
 }
 
 // Reads (and optionally clears) the fault word of the current device.

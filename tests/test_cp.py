@@ -274,11 +274,13 @@ def test_cp_emulated_ranks_backward_match_full_sequence(gdn2, world):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 4])
-def test_cp_emulated_ranks_match_full_sequence(gdn2, world):
+@pytest.mark.parametrize("world,T", [(2, 512), (4, 512), (2, 4096)])
+def test_cp_emulated_ranks_match_full_sequence(gdn2, world, T):
+    """T = 4096 over 2 ranks: 32 chunks per shard, so each shard's transition
+    runs in segments (every segment's M_s and h_s, then two folds)."""
     cp = __import__("importlib").import_module("gateddeltanet-2_b200.cp")
     be = cp.CudaBackend()
-    T, H, K, V = 512, 2, 128, 128
+    H, K, V = 2, 128, 128
     gen = torch.Generator().manual_seed(world)
     q = torch.nn.functional.normalize(torch.randn(1, T, H, K, generator=gen), dim=-1).bfloat16().cuda()
     k = torch.nn.functional.normalize(torch.randn(1, T, H, K, generator=gen), dim=-1).bfloat16().cuda()
