@@ -23,9 +23,12 @@
 //   intra: dAqk = scale do v_new^T, dT through the anchored score factors
 //   (exact per-pair path for the (block, channel)s the forward flagged)
 //   dG -> in-chunk reverse cumsum -> gate VJP; l2norm VJP on dq, dk.
+#include <type_traits>
+
 #include "common.cuh"
 #include "chunk_layout.cuh"
 #include "profile.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 
@@ -264,6 +267,73 @@ struct BIntraSmem {
   GDN2_DEV Staged& st() { return *reinterpret_cast<Staged*>(u + kStageOff); }
 };
 
+// d_k = d_v = 128: the products with the chunk's states and the WY products
+// (dq, dk, dY, dAqk, d(wv), dA, d(b k 2^G), X, dT) run on tcgen05 with M = 64
+// accumulators in TMEM, read back with the 16x256b shape straight into the
+// mma.sync fragment layout the 16 warps use for everything else.  A
+// tcgen05 product reads each operand tile from shared memory once, where 16
+// mma.sync warps read every operand four times over (ldmatrix per warp tile).
+// Their operands are 128-byte-swizzled [rows x 64] bf16 tiles (tc.cuh); the
+// anchored row / column parts keep mma.sync on padded tiles.
+template <typename TB>
+struct BIntraSmemTc {
+  static constexpr int K = 128, V = 128;
+  static constexpr int LK = K + 8, LV = V + 8, LA = kChunk + 8, LG = K + 4;
+  static constexpr int LB = K + 16 / (int)sizeof(TB);
+  static constexpr uint32_t kT = 64 * 128;  // one [64 rows x 64] bf16 swizzled tile, bytes
+  alignas(1024) unsigned char A[kT];        // (I+T)^-1 as [t][s]
+  alignas(16) float G[kChunk][LG];
+  alignas(16) __nv_bfloat16 DAqk[kChunk][LA];
+  alignas(16) __nv_bfloat16 DT[kChunk][LA];
+  alignas(16) float last[K];
+  alignas(16) float rsum[kChunk][4][2];
+  alignas(16) uint8_t flag[4][K];
+  alignas(16) float ptot[kBIntraThreads / K][K];
+  alignas(8) uint64_t bar[5];  // completion of the five tcgen05 product rounds
+  uint32_t tbase;              // TMEM base address (512 columns)
+  int nflag;
+  // tiles of 64-column blocks: [block][row][64]
+  struct P1 {
+    alignas(1024) unsigned char DVN[2 * kT];  // dv_new [t][v]
+    unsigned char DY[2 * kT];                 // -dY [t][k]
+    unsigned char HsT[4 * kT];                // h^T [v][k] (128 rows per k block)
+    unsigned char DHT[4 * kT];                // dh^T [v][k]
+    unsigned char DO[2 * kT];                 // do [t][v]
+    unsigned char VN[2 * kT];                 // v_new [t][v]
+  };
+  struct P2 {
+    alignas(1024) unsigned char DVN[2 * kT];  // as in P1
+    unsigned char DY[2 * kT];
+    unsigned char KB2G[2 * kT];  // b k 2^G [s][k] (first: dv staged for 16-byte stores)
+    unsigned char WV[2 * kT];    // w v [s][v]
+    unsigned char DA[kT];        // dA [t][u]
+    unsigned char X[kT];         // dA A^T [t][t']
+  };
+  struct P3 {
+    alignas(16) __nv_bfloat16 QG[kChunk][LK];
+    alignas(16) __nv_bfloat16 KBG[kChunk][LK];
+    alignas(16) __nv_bfloat16 KN[160][LK];
+  };
+  static constexpr size_t kStageOff =
+      ((sizeof(P2) > sizeof(P3) ? sizeof(P2) : sizeof(P3)) + 127) / 128 * 128;
+  struct Staged {
+    alignas(16) __nv_bfloat16 Q[kChunk][LK];
+    alignas(16) __nv_bfloat16 Kk[kChunk][LK];
+    alignas(16) TB Bg[kChunk][K + 16 / sizeof(TB)];
+  };
+  static constexpr size_t kUnion =
+      sizeof(P1) > kStageOff + sizeof(Staged) ? sizeof(P1) : kStageOff + sizeof(Staged);
+  alignas(1024) unsigned char u[kUnion];
+  GDN2_DEV P1& p1() { return *reinterpret_cast<P1*>(u); }
+  GDN2_DEV P2& p2() { return *reinterpret_cast<P2*>(u); }
+  GDN2_DEV P3& p3() { return *reinterpret_cast<P3*>(u); }
+  GDN2_DEV Staged& st() { return *reinterpret_cast<Staged*>(u + kStageOff); }
+};
+static_assert(sizeof(BIntraSmemTc<float>) + 1024 <= 227 * 1024, "B3 (tcgen05) shared memory");
+static_assert(offsetof(BIntraSmemTc<float>::P2, DVN) == offsetof(BIntraSmemTc<float>::P1, DVN) &&
+                  offsetof(BIntraSmemTc<float>::P2, DY) == offsetof(BIntraSmemTc<float>::P1, DY),
+              "dv_new and dY stay in place from phase 1 to phase 2");
+
 using BIntraSmem128x128 = BIntraSmem<128, 128, float>;
 static_assert(offsetof(BIntraSmem128x128, u) % 128 == 0, "cp.async/ldmatrix targets need 16B alignment");
 static_assert(sizeof(BIntraSmem128x128) <= 227 * 1024, "B3 shared memory");
@@ -286,12 +356,32 @@ GDN2_DEV float ldb(const void* p, int64_t i) {
   return to_f(static_cast<const TB*>(p)[i]);
 }
 
+__device__ unsigned int g_b3_fault;  // bit 0: a bounded wait of the backward intra kernel gave up
+
+// Bounded wait on a tcgen05 commit, with the same outcome on every lane (the
+// warp-collective TMEM loads after it must not diverge); a timeout is recorded
+// and the kernel carries on, so every thread still meets every barrier.
+GDN2_DEV void b3_wait(uint64_t* bar) {
+  const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(bar, 0));
+  if (!ok && (threadIdx.x & 31) == 0) atomicOr(&g_b3_fault, 1u);
+  tc::tc_fence_after();
+}
+GDN2_DEV uint64_t b3_kmaj(uint32_t a) { return tc::sdesc_sw128(a, 16, 1024); }
+GDN2_DEV uint64_t b3_mnmaj(uint32_t a, uint32_t lbo) { return tc::sdesc_sw128(a, lbo, 1024); }
+// bf16 pair (c even) of element (r, c) of a tile of 64-column swizzled blocks
+// `block` bytes apart
+GDN2_DEV uint32_t b3_off(int r, int c, uint32_t block) { return (c >> 6) * block + tc::sw128_off(r, c & 63); }
+
 template <int K, int V, typename TB>
 __global__ void __launch_bounds__(kBIntraThreads, 1)
 chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  using S = BIntraSmem<K, V, TB>;
-  S& sm = *reinterpret_cast<S*>(smem_raw);
+  extern __shared__ __align__(1024) unsigned char smem_b3[];
+  unsigned char* smem_raw = smem_b3;
+  constexpr bool kTc = K == 128 && V == 128;
+  using S = std::conditional_t<kTc, BIntraSmemTc<TB>, BIntraSmem<K, V, TB>>;
+  // tcgen05 operand tiles start on 1024-byte boundaries; the offset is applied to
+  // smem_raw itself so that every access stays a shared-memory access
+  S& sm = *reinterpret_cast<S*>(smem_raw + (kTc ? (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u : 0u));
   auto& p1 = sm.p1();
   auto& p2 = sm.p2();
   auto& p3 = sm.p3();
@@ -320,25 +410,46 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   {
     const __nv_bfloat16* hsrc = ws.h + (cidx * H + h) * (int64_t)K * V;
     const __nv_bfloat16* dhsrc = bw.dh + (cidx * H + h) * (int64_t)K * V;
-    for (int i = tid; i < V * (K / 8); i += kBIntraThreads) {
-      const int r = i / (K / 8), p = (i % (K / 8)) * 8;
-      cp_async16b(&p1.HsT[r][p], hsrc + (int64_t)r * K + p, true);
-      cp_async16b(&p1.DHT[r][p], dhsrc + (int64_t)r * K + p, true);
-    }
-    for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
-      const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      const bool ok = r < L;
-      const int64_t gi = tokV(ok ? r : 0, p);
-      cp_async16b(&p1.DO[r][p], dout + gi, ok);
-      cp_async16b(&p1.VN[r][p], ws.v_new + gi, ok);
-      cp_async16b(&p1.DVN[r][p], bw.dvn + gi, ok);
+    if constexpr (kTc) {
+      // swizzled tiles: 16-byte piece (r, p) of 64-column block b at b * block + sw128_off(r, p)
+      for (int i = tid; i < V * (K / 8); i += kBIntraThreads) {
+        const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+        const uint32_t o = b3_off(r, p, 2 * S::kT);  // 128 rows per block
+        cp_async16b(p1.HsT + o, hsrc + (int64_t)r * K + p, true);
+        cp_async16b(p1.DHT + o, dhsrc + (int64_t)r * K + p, true);
+      }
+      for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
+        const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+        const bool ok = r < L;
+        const int64_t gi = tokV(ok ? r : 0, p);
+        const uint32_t o = b3_off(r, p, S::kT);
+        cp_async16b(p1.DO + o, dout + gi, ok);
+        cp_async16b(p1.VN + o, ws.v_new + gi, ok);
+        cp_async16b(p1.DVN + o, bw.dvn + gi, ok);
+      }
+    } else {
+      for (int i = tid; i < V * (K / 8); i += kBIntraThreads) {
+        const int r = i / (K / 8), p = (i % (K / 8)) * 8;
+        cp_async16b(&p1.HsT[r][p], hsrc + (int64_t)r * K + p, true);
+        cp_async16b(&p1.DHT[r][p], dhsrc + (int64_t)r * K + p, true);
+      }
+      for (int i = tid; i < kChunk * (V / 8); i += kBIntraThreads) {
+        const int r = i / (V / 8), p = (i % (V / 8)) * 8;
+        const bool ok = r < L;
+        const int64_t gi = tokV(ok ? r : 0, p);
+        cp_async16b(&p1.DO[r][p], dout + gi, ok);
+        cp_async16b(&p1.VN[r][p], ws.v_new + gi, ok);
+        cp_async16b(&p1.DVN[r][p], bw.dvn + gi, ok);
+      }
     }
     cp_commit();  // group 1: the phase-1 operands
     // group 2: A and G, first needed after the phase-1 products
     for (int i = tid; i < kChunk * (kChunk / 8); i += kBIntraThreads) {
       const int r = i / (kChunk / 8), p = (i % (kChunk / 8)) * 8;
       const bool ok = r < L;
-      cp_async16b(&sm.A[r][p], ws.Akk + ((t0 + (ok ? r : 0)) * H + h) * kChunk + p, ok);
+      const __nv_bfloat16* src = ws.Akk + ((t0 + (ok ? r : 0)) * H + h) * kChunk + p;
+      if constexpr (kTc) cp_async16b(sm.A + tc::sw128_off(r, p), src, ok);
+      else cp_async16b(&sm.A[r][p], src, ok);
     }
     for (int i = tid; i < kChunk * (K / 4); i += kBIntraThreads) {
       const int r = i / (K / 4), p = (i % (K / 4)) * 4;
@@ -348,8 +459,38 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     cp_commit();
     for (int c = tid; c < K; c += kBIntraThreads) sm.last[c] = 0.f;
     if (tid == 0) sm.nflag = 0;
+    if constexpr (kTc) {
+      if (warp == 0) tc::tmem_alloc(&sm.tbase, 512);
+      if (tid == 0) {
+        for (int i = 0; i < 5; ++i) tc::mbar_init(&sm.bar[i], 1);
+        tc::mbar_fence_init();
+      }
+    }
     cp_wait<1>();
+    if constexpr (kTc) {
+      tc::fence_proxy_async();  // the copied tiles -> the tensor core's proxy
+      tc::tc_fence_before();
+    }
     __syncthreads();
+    if constexpr (kTc) {
+      tc::tc_fence_after();
+      // round 1 (TMEM columns: dq [0,128), dk [128,256), -dY [256,384), dAqk [384,448)):
+      //   dq = do h, dk = v_new dh, dY = dv_new h over v (h^T tiles as N-major B), dAqk = do v_new^T
+      if (tid == 0) {
+        constexpr uint32_t iN = tc::idesc_bf16(64, 128, 0, 1), i64 = tc::idesc_bf16(64, 64, 0, 0);
+        const uint32_t tb = sm.tbase, sH = smem_u32(p1.HsT), sDH = smem_u32(p1.DHT), sDO = smem_u32(p1.DO),
+                       sVN = smem_u32(p1.VN), sDVN = smem_u32(p1.DVN);
+#pragma unroll 1
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ko = (kk >> 2) * S::kT + (kk & 3) * 32, hk = kk * 2048;
+          tc::mma_bf16(tb + 0, b3_kmaj(sDO + ko), b3_mnmaj(sH + hk, 2 * S::kT), iN, kk > 0);
+          tc::mma_bf16(tb + 128, b3_kmaj(sVN + ko), b3_mnmaj(sDH + hk, 2 * S::kT), iN, kk > 0);
+          tc::mma_bf16(tb + 256, b3_kmaj(sDVN + ko), b3_mnmaj(sH + hk, 2 * S::kT), iN, kk > 0);
+          tc::mma_bf16(tb + 384, b3_kmaj(sDO + ko), b3_kmaj(sVN + ko), i64, kk > 0);
+        }
+        tc::mma_commit(&sm.bar[0]);
+      }
+    }
     // w and v are read from global in the d(w v) step: pull them into L2 now
     if (tid < 2 * L) {
       const int r = tid >> 1;
@@ -372,15 +513,40 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   const float* Glast = &sm.G[kChunk - 1][0];
 
   // ---- phase 1: products with h, dh ------------------------------------------
-  warp_mma<1, NTk, false, false>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
-  warp_mma<1, NTk, false, false>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DHT[0][0], S::LK}, n0, 0, V, lane);
-  {
+  // bf16 element (r, c) of the tiles both variants write: dY, w v, b k 2^G and
+  // the staged dv (padded rows for mma.sync, swizzled blocks for tcgen05)
+  auto pDY = [&](int r, int c) -> __nv_bfloat16* {
+    if constexpr (kTc) return reinterpret_cast<__nv_bfloat16*>(p1.DY + b3_off(r, c, S::kT));
+    else return &p1.DY[r][c];
+  };
+  auto pWV = [&](int r, int c) -> __nv_bfloat16* {
+    if constexpr (kTc) return reinterpret_cast<__nv_bfloat16*>(p2.WV + b3_off(r, c, S::kT));
+    else return &p2.WV[r][c];
+  };
+  auto pKB2G = [&](int r, int c) -> __nv_bfloat16* {
+    if constexpr (kTc) return reinterpret_cast<__nv_bfloat16*>(p2.KB2G + b3_off(r, c, S::kT));
+    else return &p2.KB2G[r][c];
+  };
+  // dv is staged in the b k 2^G tile (free until phase 2) for 16-byte stores
+  constexpr bool kStageDv = K == V;
+  auto pSDV = [&](int r, int c) -> __nv_bfloat16* {
+    if constexpr (kTc) return reinterpret_cast<__nv_bfloat16*>(p2.KB2G + b3_off(r, c, S::kT));
+    else return &p2.KB2G[0][0] + r * S::LV + c;
+  };
+  // this warp's TMEM lane quarter: rows [m0, m0 + 16) of every M = 64 accumulator
+  uint32_t tl = 0;
+  if constexpr (kTc) tl = tc::tmem_addr(sm.tbase, 32 * (warp & 3), 0);
+
+  if constexpr (!kTc) {
+    warp_mma<1, NTk, false, false>(dq, Smem{&p1.DO[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
+    warp_mma<1, NTk, false, false>(dk, Smem{&p1.VN[0][0], S::LV}, m0, Smem{&p1.DHT[0][0], S::LK}, n0, 0, V, lane);
     float t[1][NTk][4];
     zero_acc(t);
     warp_mma<1, NTk, false, false>(t, Smem{&p1.DVN[0][0], S::LV}, m0, Smem{&p1.HsT[0][0], S::LK}, n0, 0, V, lane);
-    acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { p1.DY[r][c] = __float2bfloat16_rn(-v); });
+    acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { *pDY(r, c) = __float2bfloat16_rn(-v); });
   }
   cp_wait<0>();  // A and G
+  if constexpr (kTc) tc::fence_proxy_async();  // A is a tcgen05 operand from round 2 on
   __syncthreads();
   // the forward's exactness flags (same criterion, same G)
   for (int i = tid; i < 4 * K; i += kBIntraThreads) {
@@ -399,7 +565,15 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll 4
     for (int v = part * kVPer; v < (part + 1) * kVPer; ++v) {
-      const float2 hh = ld2(&p1.HsT[v][r]), dd = ld2(&p1.DHT[v][r]);
+      float2 hh, dd;
+      if constexpr (kTc) {
+        const uint32_t o = b3_off(v, r, 2 * S::kT);
+        hh = ld2(reinterpret_cast<const __nv_bfloat16*>(p1.HsT + o));
+        dd = ld2(reinterpret_cast<const __nv_bfloat16*>(p1.DHT + o));
+      } else {
+        hh = ld2(&p1.HsT[v][r]);
+        dd = ld2(&p1.DHT[v][r]);
+      }
       s0 += hh.x * dd.x;
       s1 += hh.y * dd.y;
     }
@@ -409,13 +583,47 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   // dAqk = scale do v_new^T (lower incl. diagonal)
   {
     float t[1][2][4];
-    zero_acc(t);
-    warp_mma<1, 2, false, true>(t, Smem{&p1.DO[0][0], S::LV}, mm, Smem{&p1.VN[0][0], S::LV}, nn, 0, V, lane);
+    if constexpr (kTc) {
+      // round 1's accumulators: dq, dk to registers, -dY to its operand tile
+      b3_wait(&sm.bar[0]);
+      {
+        float y[1][NTk][4];
+        tc::tmem_ld_frag<NTk>(tl + 256 + n0, y[0]);
+        tc::tmem_wait_ld();
+        acc_foreach(y, m0, n0, lane, [&](float v, int r, int c) { *pDY(r, c) = __float2bfloat16_rn(-v); });
+      }
+      tc::tmem_ld_frag<NTk>(tl + 0 + n0, dq[0]);
+      tc::tmem_ld_frag<NTk>(tl + 128 + n0, dk[0]);
+      tc::tmem_ld_frag<2>(tl + 384 + nn, t[0]);
+      tc::tmem_wait_ld();
+    } else {
+      zero_acc(t);
+      warp_mma<1, 2, false, true>(t, Smem{&p1.DO[0][0], S::LV}, mm, Smem{&p1.VN[0][0], S::LV}, nn, 0, V, lane);
+    }
     acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
       sm.DAqk[r][s] = __float2bfloat16_rn((s <= r && r < L) ? v * scale : 0.f);
     });
   }
+  if constexpr (kTc) {
+    tc::fence_proxy_async();  // -dY -> the tensor core
+    tc::tc_fence_before();    // round 1's columns are drained
+  }
   __syncthreads();  // h, dh, do, v_new are dead: stage q, k, b in their place
+  if constexpr (kTc) {
+    tc::tc_fence_after();
+    // round 2: d(w v) = A^T dv_new -> columns [256,384), d(b k 2^G) = A^T dY -> [0,128)
+    // (A as an M-major operand, dv_new and dY as N-major ones)
+    if (tid == 0) {
+      constexpr uint32_t iT = tc::idesc_bf16(64, 128, 1, 1);
+      const uint32_t tb = sm.tbase, sA = smem_u32(sm.A), sDVN = smem_u32(p2.DVN), sDY = smem_u32(p2.DY);
+#pragma unroll 1
+      for (int kk = 0; kk < 4; ++kk) {
+        tc::mma_bf16(tb + 256, b3_mnmaj(sA + kk * 2048, S::kT), b3_mnmaj(sDVN + kk * 2048, S::kT), iT, kk > 0);
+        tc::mma_bf16(tb + 0, b3_mnmaj(sA + kk * 2048, S::kT), b3_mnmaj(sDY + kk * 2048, S::kT), iT, kk > 0);
+      }
+      tc::mma_commit(&sm.bar[1]);
+    }
+  }
   for (int i = tid; i < kChunk * (K / 8); i += kBIntraThreads) {
     const int r = i / (K / 8), p = (i % (K / 8)) * 8;
     const bool ok = r < L;
@@ -431,10 +639,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
   cp_commit();
   // d(w v) = A^T dv_new  ->  dv = w d(wv), dw = v d(wv); the same registers of
-  // w and v also form WV = w v for phase 2 (w, v are read from HBM once).  dv
-  // is staged in the WY operand tile (free until phase 2) for 16-byte stores.
-  constexpr bool kStageDv = K == V;
-  __nv_bfloat16 (*sdv)[S::LV] = reinterpret_cast<__nv_bfloat16 (*)[S::LV]>(&p2.KB2G[0][0]);
+  // w and v also form WV = w v for phase 2 (w, v are read from HBM once).
   {
     __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
     TB* dw = static_cast<TB*>(gr.dw);
@@ -455,19 +660,25 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         vl[j][2 * x + 1] = v2.y;
       }
     float t[1][NTv][4];
-    zero_acc(t);
-    warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
-                                  lane);
+    if constexpr (kTc) {
+      b3_wait(&sm.bar[1]);
+      tc::tmem_ld_frag<NTv>(tl + 256 + n0v, t[0]);
+      tc::tmem_wait_ld();
+    } else {
+      zero_acc(t);
+      warp_mma<1, NTv, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p1.DVN[0][0], S::LV}, n0v, 0, kChunk,
+                                    lane);
+    }
 #pragma unroll
     for (int j = 0; j < NTv; ++j)
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         const int r = m0 + (lane >> 2) + x * 8, c = n0v + 8 * j + 2 * (lane & 3);
-        *reinterpret_cast<__nv_bfloat162*>(&p2.WV[r][c]) =
+        *reinterpret_cast<__nv_bfloat162*>(pWV(r, c)) =
             __floats2bfloat162_rn(wl[j][2 * x] * vl[j][2 * x], wl[j][2 * x + 1] * vl[j][2 * x + 1]);
         const __nv_bfloat162 dv2 =
             __floats2bfloat162_rn(t[0][j][2 * x] * wl[j][2 * x], t[0][j][2 * x + 1] * wl[j][2 * x + 1]);
-        if constexpr (kStageDv) *reinterpret_cast<__nv_bfloat162*>(&sdv[r][c]) = dv2;
+        if constexpr (kStageDv) *reinterpret_cast<__nv_bfloat162*>(pSDV(r, c)) = dv2;
         if (r < L) {
           const int64_t gi = tokV(r, c);
           if constexpr (!kStageDv) *reinterpret_cast<__nv_bfloat162*>(dv + gi) = dv2;
@@ -481,7 +692,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     __nv_bfloat16* dv = static_cast<__nv_bfloat16*>(gr.dv);
     for (int i = tid; i < L * (V / 8); i += kBIntraThreads) {
       const int r = i / (V / 8), p = (i % (V / 8)) * 8;
-      *reinterpret_cast<uint4*>(dv + tokV(r, p)) = *reinterpret_cast<const uint4*>(&sdv[r][p]);
+      *reinterpret_cast<uint4*>(dv + tokV(r, p)) = *reinterpret_cast<const uint4*>(pSDV(r, p));
     }
   }
   // inter-chunk parts: dq = scale (do h^T) 2^G ; dk = (v_new dh^T) 2^(G_last - G)
@@ -531,23 +742,49 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     ld8(&sm.G[r][c0], G8);
 #pragma unroll
     for (int e = 0; e < 8; ++e) b8[e] = b8[e] * k8[e] * exp2_approx(G8[e]);
-    st8(&p2.KB2G[r][c0], b8);
+    st8(pKB2G(r, c0), b8);
   }
+  if constexpr (kTc) tc::fence_proxy_async();  // w v and b k 2^G -> the tensor core
   __syncthreads();
-  {
-    float t[1][2][4];
-    zero_acc(t);
-    warp_mma<1, 2, false, true>(t, Smem{&p2.DVN[0][0], S::LV}, mm, Smem{&p2.WV[0][0], S::LV}, nn, 0, V, lane);
-    warp_mma<1, 2, false, true>(t, Smem{&p2.DY[0][0], S::LK}, mm, Smem{&p2.KB2G[0][0], S::LK}, nn, 0, K, lane);
-    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+  float tA[1][2][4];  // dA = dv_new (w v)^T + dY (b k 2^G)^T
+  if constexpr (kTc) {
+    tc::tc_fence_after();
+    // round 3: dA -> columns [384,448)
+    if (tid == 0) {
+      constexpr uint32_t i64 = tc::idesc_bf16(64, 64, 0, 0);
+      const uint32_t tb = sm.tbase, sDVN = smem_u32(p2.DVN), sWV = smem_u32(p2.WV), sDY = smem_u32(p2.DY),
+                     sKB = smem_u32(p2.KB2G);
+#pragma unroll 1
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t ko = (kk >> 2) * S::kT + (kk & 3) * 32;
+        tc::mma_bf16(tb + 384, b3_kmaj(sDVN + ko), b3_kmaj(sWV + ko), i64, kk > 0);
+      }
+#pragma unroll 1
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t ko = (kk >> 2) * S::kT + (kk & 3) * 32;
+        tc::mma_bf16(tb + 384, b3_kmaj(sDY + ko), b3_kmaj(sKB + ko), i64, 1);
+      }
+      tc::mma_commit(&sm.bar[2]);
+    }
+  } else {
+    zero_acc(tA);
+    warp_mma<1, 2, false, true>(tA, Smem{&p2.DVN[0][0], S::LV}, mm, Smem{&p2.WV[0][0], S::LV}, nn, 0, V, lane);
+    warp_mma<1, 2, false, true>(tA, Smem{&p2.DY[0][0], S::LK}, mm, Smem{&p2.KB2G[0][0], S::LK}, nn, 0, K, lane);
+    acc_foreach(tA, mm, nn, lane, [&](float v, int r, int s) {
       p2.DA[r][s] = __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
     });
   }
-  // d(b k 2^G) = A^T dY
+  // d(b k 2^G) = A^T dY (tcgen05: round 2, complete since the d(w v) step)
   {
     float t[1][NTk][4];
-    zero_acc(t);
-    warp_mma<1, NTk, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p2.DY[0][0], S::LK}, n0, 0, kChunk, lane);
+    if constexpr (kTc) {
+      tc::tmem_ld_frag<NTk>(tl + 0 + n0, t[0]);
+      tc::tmem_wait_ld();
+    } else {
+      zero_acc(t);
+      warp_mma<1, NTk, true, false>(t, Smem{&sm.A[0][0], S::LA}, m0, Smem{&p2.DY[0][0], S::LK}, n0, 0, kChunk,
+                                    lane);
+    }
 #pragma unroll
     for (int j = 0; j < NTk; ++j)
 #pragma unroll
@@ -567,21 +804,72 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         }
       }
   }
+  if constexpr (kTc) {
+    b3_wait(&sm.bar[2]);
+    tc::tmem_ld_frag<2>(tl + 384 + nn, tA[0]);
+    tc::tmem_wait_ld();
+    acc_foreach(tA, mm, nn, lane, [&](float v, int r, int s) {
+      *reinterpret_cast<__nv_bfloat16*>(p2.DA + tc::sw128_off(r, s)) =
+          __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
+    });
+    tc::fence_proxy_async();
+  }
   __syncthreads();
   // dT = -A^T (dA A^T), strictly lower
   {
     float t[1][2][4];
-    zero_acc(t);
-    warp_mma<1, 2, false, true>(t, Smem{&p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
-    acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) { p2.X[r][s] = __float2bfloat16_rn(v); });
-    __syncthreads();
-    zero_acc(t);
-    warp_mma<1, 2, true, false>(t, Smem{&sm.A[0][0], S::LA}, mm, Smem{&p2.X[0][0], S::LA}, nn, 0, kChunk, lane);
+    if constexpr (kTc) {
+      tc::tc_fence_after();
+      const uint32_t tb = sm.tbase, sA = smem_u32(sm.A), sX = smem_u32(p2.X);
+      // round 4: X = dA A^T -> columns [448,512)
+      if (tid == 0) {
+        constexpr uint32_t i64 = tc::idesc_bf16(64, 64, 0, 0);
+        const uint32_t sDA = smem_u32(p2.DA);
+#pragma unroll 1
+        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16(tb + 448, b3_kmaj(sDA + kk * 32), b3_kmaj(sA + kk * 32), i64, kk > 0);
+        tc::mma_commit(&sm.bar[3]);
+      }
+      b3_wait(&sm.bar[3]);
+      tc::tmem_ld_frag<2>(tl + 448 + nn, t[0]);
+      tc::tmem_wait_ld();
+      acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
+        *reinterpret_cast<__nv_bfloat16*>(p2.X + tc::sw128_off(r, s)) = __float2bfloat16_rn(v);
+      });
+      tc::fence_proxy_async();
+      __syncthreads();
+      tc::tc_fence_after();
+      // round 5: A^T X -> columns [128,192) (dk's, drained after round 1)
+      if (tid == 0) {
+        constexpr uint32_t iT = tc::idesc_bf16(64, 64, 1, 1);
+#pragma unroll 1
+        for (int kk = 0; kk < 4; ++kk)
+          tc::mma_bf16(tb + 128, b3_mnmaj(sA + kk * 2048, S::kT), b3_mnmaj(sX + kk * 2048, S::kT), iT, kk > 0);
+        tc::mma_commit(&sm.bar[4]);
+      }
+      b3_wait(&sm.bar[4]);
+      tc::tmem_ld_frag<2>(tl + 128 + nn, t[0]);
+      tc::tmem_wait_ld();
+    } else {
+      zero_acc(t);
+      warp_mma<1, 2, false, true>(t, Smem{&p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
+      acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) { p2.X[r][s] = __float2bfloat16_rn(v); });
+      __syncthreads();
+      zero_acc(t);
+      warp_mma<1, 2, true, false>(t, Smem{&sm.A[0][0], S::LA}, mm, Smem{&p2.X[0][0], S::LA}, nn, 0, kChunk, lane);
+    }
     acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
       sm.DT[r][s] = __float2bfloat16_rn((s < r && r < L) ? -v : 0.f);
     });
   }
+  if constexpr (kTc) tc::tc_fence_before();
   __syncthreads();
+  if constexpr (kTc) {
+    // every product has completed and been read: release TMEM
+    if (warp == 0) {
+      tc::tc_fence_after();
+      tc::tmem_dealloc(sm.tbase, 512);
+    }
+  }
 
   // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
   for (int g = tid; g < kChunk * K / 8; g += kBIntraThreads) {
@@ -918,7 +1206,10 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
   if (a.flags & GDN2_BWD_STATE_ONLY) return 0;
   if (a.NT > 0) {
     const bool bwb = a.dtype_bw == GDN2_BF16;
-    const size_t sm3 = bwb ? sizeof(BIntraSmem<K, V, __nv_bfloat16>) : sizeof(BIntraSmem<K, V, float>);
+    constexpr bool kTc = K == 128 && V == 128;  // the tcgen05 variant (1024-byte-aligned tiles)
+    using S16 = std::conditional_t<kTc, BIntraSmemTc<__nv_bfloat16>, BIntraSmem<K, V, __nv_bfloat16>>;
+    using S32 = std::conditional_t<kTc, BIntraSmemTc<float>, BIntraSmem<K, V, float>>;
+    const size_t sm3 = (bwb ? sizeof(S16) : sizeof(S32)) + (kTc ? 1024 : 0);
     auto k3 = bwb ? chunk_bwd_intra_kernel<K, V, __nv_bfloat16> : chunk_bwd_intra_kernel<K, V, float>;
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3));
     dim3 g3((unsigned)a.NT, (unsigned)a.H);
@@ -926,6 +1217,20 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
     k3<<<g3, kBIntraThreads, sm3, s>>>(a, g, ws, bw);
     GDN2_LAUNCH_CHECK();
   }
+  return 0;
+}
+
+// Reads (and optionally clears) the fault word of the backward intra kernel.
+int b3_fault_read(int clear, unsigned int* out) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_b3_fault, sizeof(v));
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  if (clear && v) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_b3_fault, &z, sizeof(z));
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  *out = v;
   return 0;
 }
 

@@ -230,6 +230,8 @@ int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, cons
 // context-parallel transition [M | h_e] of a dense shard on the tcgen05 scan (d_k = d_v = 128)
 int scan_trans_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s);
 int tc_fault_read(int clear, unsigned int* out);
+// fault word of the backward intra kernel (chunk_bwd.cu): bit 0 = a tcgen05 wait gave up
+int b3_fault_read(int clear, unsigned int* out);
 // fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up
 int layer_fault_read(int clear, unsigned int* out);
 
