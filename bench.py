@@ -32,8 +32,9 @@ The same JSON line carries, as extra keys:
 
 ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``
 (multi-GPU through ``torch.distributed.run``; one rank per GPU).
-``--batch`` / ``--decode-seqs`` shrink the two workloads for ncu captures; a
-line measured with either changed is not a config-2 / config-3 number.
+``--batch`` / ``--decode-seqs`` / ``--heads`` shrink the two workloads for ncu
+captures; a line measured with any of them changed is not a config-2 /
+config-3 number.
 ``--impl reference`` times the reference's algorithm on the host cores (the
 oracle port: the reference has no CPU implementation of its own and its
 kernels are Triton/sm_120 CUDA); it runs on rank 0 only.
@@ -98,6 +99,9 @@ def parse():
                     help="skip the reference Triton op in the default N=1 line (its autotuning takes minutes)")
     ap.add_argument("--batch", type=int, default=B,
                     help="sequences per GPU (config 2 is 4; smaller values are for ncu captures)")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="heads per GPU; default 16/N (the strong split).  Set on one GPU it runs the shard one "
+                         "rank of a 16/heads-GPU split runs (for ncu captures of the segmented scans)")
     ap.add_argument("--decode-seqs", type=int, default=DEC_N,
                     help="decode sequences per GPU (config 3 is 256; smaller for ncu captures)")
     ap.add_argument("--layer", action="store_true",
@@ -949,7 +953,7 @@ def main():
 
     world, rank = rk.world, rk.rank
     nb, nd_total = args.batch, args.decode_seqs
-    full = nb == B and nd_total == DEC_N
+    full = nb == B and nd_total == DEC_N and args.heads is None
     cpu_base = cpu_torch = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         note("cpu baseline: oracle port")
@@ -965,6 +969,8 @@ def main():
     note("config 2")
     strong = H % world == 0
     heads = H // world if strong else H
+    if args.heads is not None:
+        heads = args.heads
     clocks = rk.clocks()
     clocks.start()
     ms, prof, tensors = measure_op(rk, nb, heads, args.steps, args.warmup, 1234 + rank)

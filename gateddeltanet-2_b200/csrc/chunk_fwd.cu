@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "chunk_layout.cuh"
 #include "profile.cuh"
+#include "tc.cuh"
 
 namespace gdn2 {
 
@@ -94,9 +95,14 @@ GDN2_DEV float ld_bw(const void* p, int64_t i) {
   return to_f(static_cast<const TB*>(p)[i]);
 }
 
+// L2 prefetch maps of F1's first operands (q, k, g, b rows of one chunk and head)
+struct IntraPrefetch {
+  CUtensorMap q, k, g, b;
+};
+
 template <int K, int V, typename TB>
 __global__ void __launch_bounds__(kIntraThreads, 1)
-chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride) {
+chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_constant__ IntraPrefetch pm) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   using S = IntraSmem<K, V>;
   S& sm = *reinterpret_cast<S*>(smem_raw);
@@ -172,23 +178,20 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride) {
   }
   // CTAs start in linear order, one per SM: the CTA pf_stride places on takes
   // this SM's slot next.  Its first operands (q, k, g, b rows) go to L2 now,
-  // behind this CTA's own loads, so its first wait reads L2 instead of HBM.
-  if (pf_stride > 0) {
-    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + pf_stride;
-    if (nxt < (int64_t)gridDim.x * gridDim.y) {
-      const int64_t nh = nxt / gridDim.x;
+  // behind this CTA's own loads, so its first wait reads L2 instead of HBM:
+  // one tensor prefetch per operand, issued by one thread.
+  if (pf_stride > 0 && tid == 0) {  // the launcher passes 0 unless linear CTA ids fit 31 bits
+    const uint32_t gx = gridDim.x, nxt = blockIdx.y * gx + blockIdx.x + (uint32_t)pf_stride;
+    if (nxt < gx * gridDim.y) {
+      const uint32_t nh = nxt / gx;
       int64_t nn, nci, nbos, nlen;
-      geo.chunk(nxt % gridDim.x, nn, nci);
+      geo.chunk(nxt - nh * gx, nn, nci);
       geo.seq(nn, nbos, nlen);
-      const int r = tid & (kChunk - 1), which = tid / kChunk;  // 4 x 64 rows
-      if (r < nlen - nci * kChunk && which < 4) {
-        const int64_t row = ((nbos + nci * kChunk + r) * H + nh) * K;
-        const int gsz = (a.flags & GDN2_G_BF16) ? 2 : 4;
-        if (which == 0) l2_prefetch(qin + row, K * 2);
-        else if (which == 1) l2_prefetch(kin + row, K * 2);
-        else if (which == 2) l2_prefetch(static_cast<const char*>(a.g) + row * gsz, K * gsz);
-        else l2_prefetch(static_cast<const TB*>(a.b) + row, K * (int)sizeof(TB));
-      }
+      const int tt = (int)(nbos + nci * kChunk), hh = (int)nh;
+      tc::tma_prefetch_3d(&pm.q, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.k, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.g, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.b, 0, hh, tt);
     }
   }
   if (l2) {
@@ -797,6 +800,18 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
 }
 
 // ---------------------------------------------------------------------------
+// F1's next-CTA prefetch: its stride (the SM count) and the maps of q, k, g, b,
+// or 0 (no prefetch) when linear CTA ids or token coordinates exceed 31 bits or
+// the driver rejects a map.  The prefetch only warms L2; results do not depend on it.
+inline int intra_prefetch(const gdn2_chunk_args& a, IntraPrefetch& pm) {
+  const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T;
+  if ((uint64_t)a.NT * a.H >= (1ull << 31) || tokens >= (1ull << 31)) return 0;
+  const bool ok = chunk_rows_map(&pm.q, a.q, 2, a.K, a.H, tokens) && chunk_rows_map(&pm.k, a.k, 2, a.K, a.H, tokens) &&
+                  chunk_rows_map(&pm.g, a.g, (a.flags & GDN2_G_BF16) ? 2 : 4, a.K, a.H, tokens) &&
+                  chunk_rows_map(&pm.b, a.b, a.dtype_bw == GDN2_BF16 ? 2 : 4, a.K, a.H, tokens);
+  return ok ? sm_count() : 0;
+}
+
 template <int K, int V>
 int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
   if (a.NT > 0 && !(a.flags & GDN2_SKIP_INTRA)) {
@@ -805,7 +820,9 @@ int launch_fwd_kv(const gdn2_chunk_args& a, const ChunkWs& ws, cudaStream_t s) {
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
     dim3 g1((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKIntra, s);
-    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, sm_count());
+    IntraPrefetch pm;
+    const int pf = intra_prefetch(a, pm);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, pf, pm);
     GDN2_LAUNCH_CHECK();
   }
   if (scan_fwd_tc_supported(a)) return scan_fwd_tc_launch(a, ws, s);
@@ -827,7 +844,9 @@ int launch_transition_kv(const gdn2_chunk_args& a, const ChunkWs& ws, float* map
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1));
     dim3 g1((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKIntra, s);
-    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, sm_count());
+    IntraPrefetch pm;
+    const int pf = intra_prefetch(a, pm);
+    k1<<<g1, kIntraThreads, sm1, s>>>(a, ws, pf, pm);
     GDN2_LAUNCH_CHECK();
   }
   // d_k = d_v = 128: the tcgen05 scan, one CTA for the M columns and one for h_e

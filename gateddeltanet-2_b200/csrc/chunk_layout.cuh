@@ -1,6 +1,8 @@
 // Layout of the chunk workspace: the forward's scratch (WY factors the scan
 // consumes) plus what the backward reads back.  Host and device share it.
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace gdn2 {
@@ -230,6 +232,9 @@ int scan_bwd_tc_launch(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, cons
 // context-parallel transition [M | h_e] of a dense shard on the tcgen05 scan (d_k = d_v = 128)
 int scan_trans_tc_launch(const gdn2_chunk_args& a, const ChunkWs& ws, float* maps, cudaStream_t s);
 int tc_fault_read(int clear, unsigned int* out);
+// [tokens, H, inner] (2- or 4-byte elements) -> unswizzled boxes of 64 tokens x inner of
+// one head, for L2 tensor prefetches of a chunk's rows (scan_tc.cu); false when rejected
+bool chunk_rows_map(CUtensorMap* m, const void* base, int elem_bytes, uint64_t inner, uint64_t H, uint64_t tokens);
 // fault word of the backward intra kernel (chunk_bwd.cu): bit 0 = a tcgen05 wait gave up
 int b3_fault_read(int clear, unsigned int* out);
 // fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up

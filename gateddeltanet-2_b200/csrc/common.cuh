@@ -299,6 +299,12 @@ struct SeqGeom {
     if (cidx) {
       n = cidx[2 * c];
       i = cidx[2 * c + 1];
+    } else if (c < (1ll << 31) && NTseq < (1ll << 31)) {
+      // 32-bit division: a short instruction sequence where the 64-bit one is a
+      // long dependent chain on every CTA's critical path
+      const uint32_t q = static_cast<uint32_t>(c) / static_cast<uint32_t>(NTseq);
+      n = q;
+      i = c - static_cast<int64_t>(q) * NTseq;
     } else {
       n = c / NTseq;
       i = c % NTseq;

@@ -1107,6 +1107,22 @@ bool rows_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows) {
 
 }  // namespace
 
+// [tokens, H, inner] of 2- or 4-byte elements -> boxes of 64 tokens x `inner` of
+// one head, unswizzled: the shape of an L2 tensor prefetch of one chunk's rows
+bool chunk_rows_map(CUtensorMap* m, const void* base, int elem_bytes, uint64_t inner, uint64_t H, uint64_t tokens) {
+  auto enc = encode_fn();
+  if (!enc || !base || inner > 256 || (elem_bytes != 2 && elem_bytes != 4)) return false;
+  const uint64_t eb = (uint64_t)elem_bytes;
+  cuuint64_t dims[3] = {inner, H, tokens};
+  cuuint64_t strides[2] = {inner * eb, H * inner * eb};
+  cuuint32_t box[3] = {(cuuint32_t)inner, 1, 64};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+             const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool scan_fwd_tc_supported(const gdn2_chunk_args& a) { return a.K == kTcK && a.V == kTcV; }
 
 namespace {
