@@ -372,9 +372,16 @@ GDN2_DEV uint64_t b3_mnmaj(uint32_t a, uint32_t lbo) { return tc::sdesc_sw128(a,
 // `block` bytes apart
 GDN2_DEV uint32_t b3_off(int r, int c, uint32_t block) { return (c >> 6) * block + tc::sw128_off(r, c & 63); }
 
+// L2 prefetch maps of the backward intra kernel's first operands: the chunk's
+// states h, dh, its do, v_new, dv_new rows, A and G
+struct BwdIntraPrefetch {
+  CUtensorMap h, dh, dout, vn, dvn, A, G;
+};
+
 template <int K, int V, typename TB>
 __global__ void __launch_bounds__(kBIntraThreads, 1)
-chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw) {
+chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs bw, int pf_stride,
+                       const __grid_constant__ BwdIntraPrefetch pm) {
   extern __shared__ __align__(1024) unsigned char smem_b3[];
   unsigned char* smem_raw = smem_b3;
   constexpr bool kTc = K == 128 && V == 128;
@@ -872,6 +879,27 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
 
   // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
+  // CTAs start in linear order, one per SM: the CTA pf_stride places on takes
+  // this SM's slot next.  Its first operands go to L2 now, while this CTA has no
+  // loads of its own in flight: one tensor prefetch each, issued by one thread.
+  if (pf_stride > 0 && tid == 0) {  // the launcher passes 0 unless linear CTA ids fit 31 bits
+    const uint32_t gx = gridDim.x, nxt = blockIdx.y * gx + blockIdx.x + (uint32_t)pf_stride;
+    if (nxt < gx * gridDim.y) {
+      const uint32_t nh = nxt / gx;
+      int64_t nn, nci, nbos, nlen;
+      geo.chunk(nxt - nh * gx, nn, nci);
+      geo.seq(nn, nbos, nlen);
+      const int tt = (int)(nbos + nci * kChunk), hh = (int)nh;
+      const int hrow = (int)(((geo.chunk0(nn) + nci) * H + nh) * V);
+      tc::tma_prefetch_2d(&pm.h, 0, hrow);
+      tc::tma_prefetch_2d(&pm.dh, 0, hrow);
+      tc::tma_prefetch_3d(&pm.dout, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.vn, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.dvn, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.A, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.G, 0, hh, tt);
+    }
+  }
   for (int g = tid; g < kChunk * K / 8; g += kBIntraThreads) {
     const int r = g / (K / 8), c0 = (g % (K / 8)) * 8;
     const int blk = r >> 4, a0 = blk * 16;
@@ -1212,9 +1240,20 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
     const size_t sm3 = (bwb ? sizeof(S16) : sizeof(S32)) + (kTc ? 1024 : 0);
     auto k3 = bwb ? chunk_bwd_intra_kernel<K, V, __nv_bfloat16> : chunk_bwd_intra_kernel<K, V, float>;
     GDN2_CUDA_TRY(cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3));
+    // next-CTA L2 prefetch (0: off) when linear CTA ids, token and state-row
+    // coordinates fit 31 bits and the driver accepts every map; it only warms L2
+    BwdIntraPrefetch pm;
+    const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T, hrows = (uint64_t)a.NT * a.H * V;
+    const bool pf_ok = (uint64_t)a.NT * a.H < (1ull << 31) && tokens < (1ull << 31) && hrows < (1ull << 31) &&
+                       state_rows_map(&pm.h, ws.h, K, hrows) && state_rows_map(&pm.dh, bw.dh, K, hrows) &&
+                       chunk_rows_map(&pm.dout, g.dout, 2, V, a.H, tokens) &&
+                       chunk_rows_map(&pm.vn, ws.v_new, 2, V, a.H, tokens) &&
+                       chunk_rows_map(&pm.dvn, bw.dvn, 2, V, a.H, tokens) &&
+                       chunk_rows_map(&pm.A, ws.Akk, 2, kChunk, a.H, tokens) &&
+                       chunk_rows_map(&pm.G, ws.G, 4, K, a.H, tokens);
     dim3 g3((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKBwdIntra, s);
-    k3<<<g3, kBIntraThreads, sm3, s>>>(a, g, ws, bw);
+    k3<<<g3, kBIntraThreads, sm3, s>>>(a, g, ws, bw, pf_ok ? sm_count() : 0, pm);
     GDN2_LAUNCH_CHECK();
   }
   return 0;

@@ -235,6 +235,8 @@ int tc_fault_read(int clear, unsigned int* out);
 // [tokens, H, inner] (2- or 4-byte elements) -> unswizzled boxes of 64 tokens x inner of
 // one head, for L2 tensor prefetches of a chunk's rows (scan_tc.cu); false when rejected
 bool chunk_rows_map(CUtensorMap* m, const void* base, int elem_bytes, uint64_t inner, uint64_t H, uint64_t tokens);
+// [rows, inner] bf16 -> unswizzled boxes of 128 rows x inner (L2 prefetches of a chunk's state)
+bool state_rows_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows);
 // fault word of the backward intra kernel (chunk_bwd.cu): bit 0 = a tcgen05 wait gave up
 int b3_fault_read(int clear, unsigned int* out);
 // fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up

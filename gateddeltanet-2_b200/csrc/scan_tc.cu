@@ -1123,6 +1123,20 @@ bool chunk_rows_map(CUtensorMap* m, const void* base, int elem_bytes, uint64_t i
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows, inner] bf16 -> unswizzled boxes of 128 rows x inner (one chunk's state of
+// 128 value rows), for L2 tensor prefetches; false when rejected
+bool state_rows_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows) {
+  auto enc = encode_fn();
+  if (!enc || !base || inner > 256) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {(cuuint32_t)inner, 128};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool scan_fwd_tc_supported(const gdn2_chunk_args& a) { return a.K == kTcK && a.V == kTcV; }
 
 namespace {
