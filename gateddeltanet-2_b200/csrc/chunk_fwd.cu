@@ -176,24 +176,6 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
       for (int e = 0; e < 8; ++e) breg[u][e] = 0.f;
     }
   }
-  // CTAs start in linear order, one per SM: the CTA pf_stride places on takes
-  // this SM's slot next.  Its first operands (q, k, g, b rows) go to L2 now,
-  // behind this CTA's own loads, so its first wait reads L2 instead of HBM:
-  // one tensor prefetch per operand, issued by one thread.
-  if (pf_stride > 0 && tid == 0) {  // the launcher passes 0 unless linear CTA ids fit 31 bits
-    const uint32_t gx = gridDim.x, nxt = blockIdx.y * gx + blockIdx.x + (uint32_t)pf_stride;
-    if (nxt < gx * gridDim.y) {
-      const uint32_t nh = nxt / gx;
-      int64_t nn, nci, nbos, nlen;
-      geo.chunk(nxt - nh * gx, nn, nci);
-      geo.seq(nn, nbos, nlen);
-      const int tt = (int)(nbos + nci * kChunk), hh = (int)nh;
-      tc::tma_prefetch_3d(&pm.q, 0, hh, tt);
-      tc::tma_prefetch_3d(&pm.k, 0, hh, tt);
-      tc::tma_prefetch_3d(&pm.g, 0, hh, tt);
-      tc::tma_prefetch_3d(&pm.b, 0, hh, tt);
-    }
-  }
   if (l2) {
     // warp w owns rows 8w..8w+7.  A lane owns 4 consecutive channels of a row
     // (kLpr lanes per row, kRpi rows per pass over the warp): pass 1 forms all
@@ -347,6 +329,25 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
   __syncthreads();
 
   // ---- 4. scores on tensor cores -------------------------------------------
+  // CTAs start in linear order, one per SM: the CTA pf_stride places on takes
+  // this SM's slot next.  Its first operands (q, k, g, b rows) go to L2 now,
+  // after this CTA's own first loads and before it requests w, v, so that its
+  // first wait reads L2 instead of HBM: one tensor prefetch per operand, issued
+  // by one thread (at the kernel's start it measured 6 us slower per launch).
+  if (pf_stride > 0 && tid == 0) {  // the launcher passes 0 unless linear CTA ids fit 31 bits
+    const uint32_t gx = gridDim.x, nxt = blockIdx.y * gx + blockIdx.x + (uint32_t)pf_stride;
+    if (nxt < gx * gridDim.y) {
+      const uint32_t nh = nxt / gx;
+      int64_t nn, nci, nbos, nlen;
+      geo.chunk(nxt - nh * gx, nn, nci);
+      geo.seq(nn, nbos, nlen);
+      const int tt = (int)(nbos + nci * kChunk), hh = (int)nh;
+      tc::tma_prefetch_3d(&pm.q, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.k, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.g, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.b, 0, hh, tt);
+    }
+  }
   // tiles (i, j <= i) for Aqk and T: 20 tiles of 16x16 over 8 warps
   for (int tile = warp; tile < 20; tile += 8) {
     const int mat = tile & 1;  // 0: Aqk, 1: T
