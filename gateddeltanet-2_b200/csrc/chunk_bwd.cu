@@ -376,6 +376,7 @@ GDN2_DEV uint32_t b3_off(int r, int c, uint32_t block) { return (c >> 6) * block
 // states h, dh, its do, v_new, dv_new rows, A and G
 struct BwdIntraPrefetch {
   CUtensorMap h, dh, dout, vn, dvn, A, G;
+  CUtensorMap q, k, b, w, v, g;  // and this CTA's own later operands
 };
 
 template <int K, int V, typename TB>
@@ -498,11 +499,15 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
         tc::mma_commit(&sm.bar[0]);
       }
     }
-    // w and v are read from global in the d(w v) step: pull them into L2 now
-    if (tid < 2 * L) {
-      const int r = tid >> 1;
-      if (tid & 1) l2_prefetch(vin + tokV(r, 0), V * 2);
-      else l2_prefetch(static_cast<const TB*>(a.w) + tokV(r, 0), V * (int)sizeof(TB));
+    // q, k, b (staged after phase 1) and w, v (read from global in the d(w v)
+    // step) go to L2 now: one tensor prefetch each, from one thread
+    if (pf_stride > 0 && tid == 0) {
+      const int tt = (int)t0, hh = (int)h;
+      tc::tma_prefetch_3d(&pm.q, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.k, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.b, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.w, 0, hh, tt);
+      tc::tma_prefetch_3d(&pm.v, 0, hh, tt);
     }
   }
 
@@ -1076,10 +1081,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   constexpr int kGParts = kBIntraThreads / K, kGRows = kChunk / kGParts;
   const bool gate = a.flags & GDN2_GATE_IN_KERNEL;
   const bool g16 = a.flags & GDN2_G_BF16;
-  if (gate && tid < L) {
-    if (g16) l2_prefetch(static_cast<const __nv_bfloat16*>(a.g) + tokK(tid, 0), K * 2);
-    else l2_prefetch(static_cast<const float*>(a.g) + tokK(tid, 0), K * 4);
-  }
+  if (gate && pf_stride > 0 && tid == 0) tc::tma_prefetch_3d(&pm.g, 0, (int)h, (int)t0);
   {
     // staged in the phase-3 operand region (dead now), written out below
     __nv_bfloat16 (*sdq)[S::LK] = reinterpret_cast<__nv_bfloat16 (*)[S::LK]>(&p3.QG[0][0]);
@@ -1250,7 +1252,13 @@ int launch_bwd_kv(const gdn2_chunk_args& a, const gdn2_chunk_grads& g, const Chu
                        chunk_rows_map(&pm.vn, ws.v_new, 2, V, a.H, tokens) &&
                        chunk_rows_map(&pm.dvn, bw.dvn, 2, V, a.H, tokens) &&
                        chunk_rows_map(&pm.A, ws.Akk, 2, kChunk, a.H, tokens) &&
-                       chunk_rows_map(&pm.G, ws.G, 4, K, a.H, tokens);
+                       chunk_rows_map(&pm.G, ws.G, 4, K, a.H, tokens) &&
+                       chunk_rows_map(&pm.q, ws.qn, 2, K, a.H, tokens) &&
+                       chunk_rows_map(&pm.k, ws.kn, 2, K, a.H, tokens) &&
+                       chunk_rows_map(&pm.b, a.b, a.dtype_bw == GDN2_BF16 ? 2 : 4, K, a.H, tokens) &&
+                       chunk_rows_map(&pm.w, a.w, a.dtype_bw == GDN2_BF16 ? 2 : 4, V, a.H, tokens) &&
+                       chunk_rows_map(&pm.v, a.v, 2, V, a.H, tokens) &&
+                       chunk_rows_map(&pm.g, a.g, (a.flags & GDN2_G_BF16) ? 2 : 4, K, a.H, tokens);
     dim3 g3((unsigned)a.NT, (unsigned)a.H);
     ProfScope ps(kKBwdIntra, s);
     k3<<<g3, kBIntraThreads, sm3, s>>>(a, g, ws, bw, pf_ok ? sm_count() : 0, pm);
