@@ -98,6 +98,7 @@ GDN2_DEV float ld_bw(const void* p, int64_t i) {
 // L2 prefetch maps of F1's first operands (q, k, g, b rows of one chunk and head)
 struct IntraPrefetch {
   CUtensorMap q, k, g, b;
+  CUtensorMap w, v;  // this CTA's own w, v rows (copied in after the scores)
 };
 
 template <int K, int V, typename TB>
@@ -158,6 +159,11 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
     }
   }
   cp_async_commit();
+  // this CTA's w, v rows, copied in after the scores, go to L2 meanwhile
+  if (pf_stride > 0 && tid == 0) {
+    tc::tma_prefetch_3d(&pm.w, 0, (int)h, (int)t0);
+    tc::tma_prefetch_3d(&pm.v, 0, (int)h, (int)t0);
+  }
   cp_async_wait<0>();
   __syncthreads();
   // Only q, k and g gate the first steps.  b (registers, needed from step 3)
@@ -809,7 +815,9 @@ inline int intra_prefetch(const gdn2_chunk_args& a, IntraPrefetch& pm) {
   if ((uint64_t)a.NT * a.H >= (1ull << 31) || tokens >= (1ull << 31)) return 0;
   const bool ok = chunk_rows_map(&pm.q, a.q, 2, a.K, a.H, tokens) && chunk_rows_map(&pm.k, a.k, 2, a.K, a.H, tokens) &&
                   chunk_rows_map(&pm.g, a.g, (a.flags & GDN2_G_BF16) ? 2 : 4, a.K, a.H, tokens) &&
-                  chunk_rows_map(&pm.b, a.b, a.dtype_bw == GDN2_BF16 ? 2 : 4, a.K, a.H, tokens);
+                  chunk_rows_map(&pm.b, a.b, a.dtype_bw == GDN2_BF16 ? 2 : 4, a.K, a.H, tokens) &&
+                  chunk_rows_map(&pm.w, a.w, a.dtype_bw == GDN2_BF16 ? 2 : 4, a.V, a.H, tokens) &&
+                  chunk_rows_map(&pm.v, a.v, 2, a.V, a.H, tokens);
   return ok ? sm_count() : 0;
 }
 
