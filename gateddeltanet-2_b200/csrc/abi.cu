@@ -70,11 +70,12 @@ const char* gdn2_status_string(int s) {
 
 int gdn2_device_fault_read(int clear, unsigned int* out) {
   if (!out) return GDN2_ERR_NULL_POINTER;
-  unsigned int a = 0, b = 0, c = 0;
+  unsigned int a = 0, b = 0, c = 0, d = 0;
   int st = gdn2::tc_fault_read(clear, &a);
   if (st == 0) st = gdn2::b3_fault_read(clear, &c);
+  if (st == 0) st = gdn2::f1_fault_read(clear, &d);
   if (st == 0) st = gdn2::layer_fault_read(clear, &b);
-  *out = a | b | c;
+  *out = a | b | c | d;
   return st;
 }
 

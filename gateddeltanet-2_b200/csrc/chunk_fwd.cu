@@ -79,6 +79,7 @@ struct IntraSmem {
   alignas(16) float Dblk[4][K];          // 2^(G_{a_i} - G_{a_{i-1}}) per anchor
   alignas(16) uint8_t flag[4][K];        // (block, channel) too wide for the anchored path
   int nflag[4];
+  alignas(8) uint64_t wv_bar;             // the TMA copies of w, v have landed
 };
 
 using IntraSmem128x128 = IntraSmem<128, 128>;
@@ -95,10 +96,12 @@ GDN2_DEV float ld_bw(const void* p, int64_t i) {
   return to_f(static_cast<const TB*>(p)[i]);
 }
 
+__device__ unsigned int g_f1_fault;  // bit 0: the bounded wait on the w, v copies gave up
+
 // L2 prefetch maps of F1's first operands (q, k, g, b rows of one chunk and head)
 struct IntraPrefetch {
   CUtensorMap q, k, g, b;
-  CUtensorMap w, v;  // this CTA's own w, v rows (copied in after the scores)
+  CUtensorMap w, v;  // this CTA's own w, v rows: an L2 prefetch, then the TMA copy after the scores
 };
 
 template <int K, int V, typename TB>
@@ -111,6 +114,10 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
   const int64_t H = a.H;
   const int64_t h = blockIdx.y;
   const int64_t cglob = blockIdx.x;
+  if (tid == 0) {
+    tc::mbar_init(&sm.wv_bar, 1);
+    tc::mbar_fence_init();
+  }
   SeqGeom geo{a.cu_seqlens, a.chunk_index, a.chunk_offset, a.T, (a.T + kChunk - 1) / kChunk};
   int64_t n, ci, bos, len;
   geo.chunk(cglob, n, ci);
@@ -383,6 +390,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
     sm.Aqk[r][s] = 0.f;
     sm.Tm[r][s] = 0.f;
   }
+  tc::fence_proxy_async();  // the score operands' reads precede the TMA writes of w, v over them
   __syncthreads();
 
   // w (TB) and v (bf16) into the score-operand region, dead until step 7's
@@ -391,7 +399,15 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
   constexpr bool kStageWV = kChunk * V * (sizeof(TB) + 2) <= sizeof(sm.u);
   TB* wst = reinterpret_cast<TB*>(&sm.u.s.QG[0][0]);  // [64][V] TB
   __nv_bfloat16* vst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(wst) + kChunk * V * sizeof(TB));
-  if constexpr (kStageWV) {
+  const bool wv_tma = kStageWV && pf_stride > 0;  // the maps were encoded (they double as TMA maps)
+  if (wv_tma) {
+    // one thread copies both [64 x V] tiles (dense rows, the layout the maps describe)
+    if (tid == 0) {
+      tc::mbar_arrive_expect_tx(&sm.wv_bar, kChunk * V * (uint32_t)(sizeof(TB) + 2));
+      tc::tma_load_3d(wst, &pm.w, &sm.wv_bar, 0, (int)h, (int)t0);
+      tc::tma_load_3d(vst, &pm.v, &sm.wv_bar, 0, (int)h, (int)t0);
+    }
+  } else if constexpr (kStageWV) {
     constexpr int kWPer16 = 16 / sizeof(TB);
     for (int i = tid; i < kChunk * (V / kWPer16); i += kIntraThreads) {
       const int r = i / (V / kWPer16), p = (i % (V / kWPer16)) * kWPer16;
@@ -512,7 +528,19 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
     }
   }
   // w v for the U product; rows past the sequence end are zero
-  cp_async_wait<0>();
+  if (wv_tma) {
+    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&sm.wv_bar, 0));
+    if (!ok && lane == 0) atomicOr(&g_f1_fault, 1u);
+    if (L < kChunk) {  // the tiles' rows past the sequence end hold the next sequence's tokens
+      for (int i = tid; i < (kChunk - L) * V; i += kIntraThreads) {
+        const int r = L + i / V, c = i % V;
+        wst[r * V + c] = TB(0.f);
+        vst[r * V + c] = __float2bfloat16_rn(0.f);
+      }
+    }
+  } else {
+    cp_async_wait<0>();
+  }
   __syncthreads();
   for (int g = tid; g < kChunk * V / 8; g += kIntraThreads) {
     const int r = g / (V / 8), c0 = (g % (V / 8)) * 8;
@@ -810,6 +838,20 @@ chunk_scan_fwd_kernel(gdn2_chunk_args a, ChunkWs ws, float* maps) {
 // F1's next-CTA prefetch: its stride (the SM count) and the maps of q, k, g, b,
 // or 0 (no prefetch) when linear CTA ids or token coordinates exceed 31 bits or
 // the driver rejects a map.  The prefetch only warms L2; results do not depend on it.
+// Reads (and optionally clears) the fault word of the forward intra kernel.
+int f1_fault_read(int clear, unsigned int* out) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_f1_fault, sizeof(v));
+  if (e != cudaSuccess) return -static_cast<int>(e);
+  if (clear && v) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_f1_fault, &z, sizeof(z));
+    if (e != cudaSuccess) return -static_cast<int>(e);
+  }
+  *out = v;
+  return 0;
+}
+
 inline int intra_prefetch(const gdn2_chunk_args& a, IntraPrefetch& pm) {
   const uint64_t tokens = (uint64_t)a.B * (uint64_t)a.T;
   if ((uint64_t)a.NT * a.H >= (1ull << 31) || tokens >= (1ull << 31)) return 0;

@@ -239,6 +239,8 @@ bool chunk_rows_map(CUtensorMap* m, const void* base, int elem_bytes, uint64_t i
 bool state_rows_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows);
 // fault word of the backward intra kernel (chunk_bwd.cu): bit 0 = a tcgen05 wait gave up
 int b3_fault_read(int clear, unsigned int* out);
+// fault word of the forward intra kernel (chunk_fwd.cu): bit 0 = its wait on the w, v copies gave up
+int f1_fault_read(int clear, unsigned int* out);
 // fault word of the layer kernels (layer.cu): bit 1 = a staging wait gave up
 int layer_fault_read(int clear, unsigned int* out);
 

@@ -351,7 +351,7 @@ int gdn2_profile_read(gdn2_kernel_stat* out, int max_entries);
 /* Fault word of the current device (no reference counterpart).  The
  * tensor-core kernels and the layer's staging kernels bound every wait on a
  * barrier; a wait that gives up abandons its work, sets a bit of this word
- * (bit 0: tensor-core scan or backward intra kernel, bit 1: layer prep) and
+ * (bit 0: tensor-core scan or an intra-chunk kernel, bit 1: layer prep) and
  * returns, leaving the context usable.  Writes the word to *out (after a device sync the caller performs)
  * and clears it when clear != 0.  Returns 0 or a negative CUDA error. */
 int gdn2_device_fault_read(int clear, unsigned int* out);
