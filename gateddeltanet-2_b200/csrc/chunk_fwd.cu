@@ -131,6 +131,9 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
   const __nv_bfloat16* vin = static_cast<const __nv_bfloat16*>(a.v);
 
   // ---- 1. stage q, k (bf16) and raw g (fp32) with cp.async; l2norm in smem -
+  // (fp32 g by TMA when the maps were encoded; the w, v copy then uses phase 1)
+  const bool g_tma = !(a.flags & GDN2_G_BF16) && pf_stride > 0;
+  const uint32_t wv_par = g_tma ? 1u : 0u;
   for (int i = tid; i < kChunk * (K / 8); i += kIntraThreads) {
     const int r = i / (K / 8), p = (i % (K / 8)) * 8;
     const bool ok = r < L;
@@ -157,6 +160,13 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
       *reinterpret_cast<float4*>(&sm.G[r][p]) = make_float4(x[0], x[1], x[2], x[3]);
       *reinterpret_cast<float4*>(&sm.G[r][p + 4]) = make_float4(x[4], x[5], x[6], x[7]);
     }
+  } else if (g_tma) {
+    // fp32 g: one TMA copy of the dense [64 x K] tile (barrier phase 0; rows
+    // past the sequence end are ignored by the cumsum, which overwrites them)
+    if (tid == 0) {
+      tc::mbar_arrive_expect_tx(&sm.wv_bar, kChunk * K * 4);
+      tc::tma_load_3d(&sm.G[0][0], &pm.g, &sm.wv_bar, 0, (int)h, (int)t0);
+    }
   } else {
     const float* gin = static_cast<const float*>(a.g);
     for (int i = tid; i < kChunk * (K / 4); i += kIntraThreads) {
@@ -172,7 +182,11 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
     tc::tma_prefetch_3d(&pm.v, 0, (int)h, (int)t0);
   }
   cp_async_wait<0>();
-  __syncthreads();
+  __syncthreads();  // also: the barrier's initialisation is visible to every thread
+  if (g_tma) {
+    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&sm.wv_bar, 0));
+    if (!ok && lane == 0) atomicOr(&g_f1_fault, 1u);
+  }
   // Only q, k and g gate the first steps.  b (registers, needed from step 3)
   // is requested now and w, v (needed by the last product) once the score
   // operands are dead (after step 4), so their HBM traffic overlaps compute
@@ -529,7 +543,7 @@ chunk_intra_kernel(gdn2_chunk_args a, ChunkWs ws, int pf_stride, const __grid_co
   }
   // w v for the U product; rows past the sequence end are zero
   if (wv_tma) {
-    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&sm.wv_bar, 0));
+    const bool ok = __all_sync(0xffffffffu, tc::mbar_wait(&sm.wv_bar, wv_par));
     if (!ok && lane == 0) atomicOr(&g_f1_fault, 1u);
     if (L < kChunk) {  // the tiles' rows past the sequence end hold the next sequence's tokens
       for (int i = tid; i < (kChunk - L) * V; i += kIntraThreads) {
