@@ -268,13 +268,14 @@ struct BIntraSmem {
 };
 
 // d_k = d_v = 128: the products with the chunk's states and the WY products
-// (dq, dk, dY, dAqk, d(wv), dA, d(b k 2^G), X, dT) run on tcgen05 with M = 64
+// (dq, dk, dY, dAqk, d(wv), dA, d(b k 2^G)) run on tcgen05 with M = 64
 // accumulators in TMEM, read back with the 16x256b shape straight into the
 // mma.sync fragment layout the 16 warps use for everything else.  A
 // tcgen05 product reads each operand tile from shared memory once, where 16
 // mma.sync warps read every operand four times over (ldmatrix per warp tile).
 // Their operands are 128-byte-swizzled [rows x 64] bf16 tiles (tc.cuh); the
-// anchored row / column parts keep mma.sync on padded tiles.
+// 64 x 64 x 64 products X = dA A^T and A^T X run on mma.sync from those same
+// swizzled tiles, the anchored row / column parts on padded tiles.
 template <typename TB>
 struct BIntraSmemTc {
   static constexpr int K = 128, V = 128;
@@ -289,7 +290,7 @@ struct BIntraSmemTc {
   alignas(16) float rsum[kChunk][4][2];
   alignas(16) uint8_t flag[4][K];
   alignas(16) float ptot[kBIntraThreads / K][K];
-  alignas(8) uint64_t bar[5];  // completion of the five tcgen05 product rounds
+  alignas(8) uint64_t bar[3];  // completion of the three tcgen05 product rounds
   uint32_t tbase;              // TMEM base address (512 columns)
   int nflag;
   // tiles of 64-column blocks: [block][row][64]
@@ -366,6 +367,13 @@ GDN2_DEV void b3_wait(uint64_t* bar) {
   if (!ok && (threadIdx.x & 31) == 0) atomicOr(&g_b3_fault, 1u);
   tc::tc_fence_after();
 }
+// a [64 x 64] bf16 tile in the 128-byte-swizzled layout, as an mma.sync operand
+struct SmemSw {
+  unsigned char* p;
+  GDN2_DEV __nv_bfloat16* at(int r, int c) const {
+    return reinterpret_cast<__nv_bfloat16*>(p + tc::sw128_off(r, c));
+  }
+};
 GDN2_DEV uint64_t b3_kmaj(uint32_t a) { return tc::sdesc_sw128(a, 16, 1024); }
 GDN2_DEV uint64_t b3_mnmaj(uint32_t a, uint32_t lbo) { return tc::sdesc_sw128(a, lbo, 1024); }
 // bf16 pair (c even) of element (r, c) of a tile of 64-column swizzled blocks
@@ -470,7 +478,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     if constexpr (kTc) {
       if (warp == 0) tc::tmem_alloc(&sm.tbase, 512);
       if (tid == 0) {
-        for (int i = 0; i < 5; ++i) tc::mbar_init(&sm.bar[i], 1);
+        for (int i = 0; i < 3; ++i) tc::mbar_init(&sm.bar[i], 1);
         tc::mbar_fence_init();
       }
     }
@@ -820,6 +828,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     b3_wait(&sm.bar[2]);
     tc::tmem_ld_frag<2>(tl + 384 + nn, tA[0]);
     tc::tmem_wait_ld();
+    tc::tc_fence_before();  // the last TMEM read: the allocation is released after the next barrier
     acc_foreach(tA, mm, nn, lane, [&](float v, int r, int s) {
       *reinterpret_cast<__nv_bfloat16*>(p2.DA + tc::sw128_off(r, s)) =
           __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
@@ -827,40 +836,26 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     tc::fence_proxy_async();
   }
   __syncthreads();
-  // dT = -A^T (dA A^T), strictly lower
+  if constexpr (kTc) {
+    // every tcgen05 product has completed and been read: release TMEM
+    if (warp == 0) {
+      tc::tc_fence_after();
+      tc::tmem_dealloc(sm.tbase, 512);
+    }
+  }
+  // dT = -A^T (dA A^T), strictly lower (64 x 64 x 64 products: mma.sync, also on
+  // the swizzled tiles, where a tcgen05 round trip costs more than it saves)
   {
     float t[1][2][4];
     if constexpr (kTc) {
-      tc::tc_fence_after();
-      const uint32_t tb = sm.tbase, sA = smem_u32(sm.A), sX = smem_u32(p2.X);
-      // round 4: X = dA A^T -> columns [448,512)
-      if (tid == 0) {
-        constexpr uint32_t i64 = tc::idesc_bf16(64, 64, 0, 0);
-        const uint32_t sDA = smem_u32(p2.DA);
-#pragma unroll 1
-        for (int kk = 0; kk < 4; ++kk) tc::mma_bf16(tb + 448, b3_kmaj(sDA + kk * 32), b3_kmaj(sA + kk * 32), i64, kk > 0);
-        tc::mma_commit(&sm.bar[3]);
-      }
-      b3_wait(&sm.bar[3]);
-      tc::tmem_ld_frag<2>(tl + 448 + nn, t[0]);
-      tc::tmem_wait_ld();
+      zero_acc(t);
+      warp_mma<1, 2, false, true>(t, SmemSw{p2.DA}, mm, SmemSw{sm.A}, nn, 0, kChunk, lane);
       acc_foreach(t, mm, nn, lane, [&](float v, int r, int s) {
         *reinterpret_cast<__nv_bfloat16*>(p2.X + tc::sw128_off(r, s)) = __float2bfloat16_rn(v);
       });
-      tc::fence_proxy_async();
       __syncthreads();
-      tc::tc_fence_after();
-      // round 5: A^T X -> columns [128,192) (dk's, drained after round 1)
-      if (tid == 0) {
-        constexpr uint32_t iT = tc::idesc_bf16(64, 64, 1, 1);
-#pragma unroll 1
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_bf16(tb + 128, b3_mnmaj(sA + kk * 2048, S::kT), b3_mnmaj(sX + kk * 2048, S::kT), iT, kk > 0);
-        tc::mma_commit(&sm.bar[4]);
-      }
-      b3_wait(&sm.bar[4]);
-      tc::tmem_ld_frag<2>(tl + 128 + nn, t[0]);
-      tc::tmem_wait_ld();
+      zero_acc(t);
+      warp_mma<1, 2, true, false>(t, SmemSw{sm.A}, mm, SmemSw{p2.X}, nn, 0, kChunk, lane);
     } else {
       zero_acc(t);
       warp_mma<1, 2, false, true>(t, Smem{&p2.DA[0][0], S::LA}, mm, Smem{&sm.A[0][0], S::LA}, nn, 0, kChunk, lane);
@@ -873,15 +868,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       sm.DT[r][s] = __float2bfloat16_rn((s < r && r < L) ? -v : 0.f);
     });
   }
-  if constexpr (kTc) tc::tc_fence_before();
   __syncthreads();
-  if constexpr (kTc) {
-    // every product has completed and been read: release TMEM
-    if (warp == 0) {
-      tc::tc_fence_after();
-      tc::tmem_dealloc(sm.tbase, 512);
-    }
-  }
 
   // ---- phase 3: intra-chunk VJP through the anchored scores --------------------
   // CTAs start in linear order, one per SM: the CTA pf_stride places on takes

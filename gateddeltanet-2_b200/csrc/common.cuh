@@ -148,8 +148,8 @@ struct Smem {
 
 // A fragment (16x16 slice of the logical A[m][k]) at (m0, k0).
 // kTrans=false: A stored row-major [m][k]; true: stored [k][m] (use A^T of a stored matrix).
-template <bool kTrans>
-GDN2_DEV void load_a(uint32_t* a, Smem s, int m0, int k0, int lane) {
+template <bool kTrans, typename SM>
+GDN2_DEV void load_a(uint32_t* a, SM s, int m0, int k0, int lane) {
   if (!kTrans) {
     const int r = m0 + (lane & 7) + ((lane >> 3) & 1) * 8;
     const int c = k0 + (lane >> 4) * 8;
@@ -164,8 +164,8 @@ GDN2_DEV void load_a(uint32_t* a, Smem s, int m0, int k0, int lane) {
 // Two B fragments (k 16 x n 16 of the logical B[k][n]) at (k0, n0): b[0..1] for
 // n0..n0+7 and b[2..3] for n0+8..n0+15.
 // kNK=false: B stored row-major [k][n]; true: stored [n][k] (B^T row-major).
-template <bool kNK>
-GDN2_DEV void load_b2(uint32_t* b, Smem s, int k0, int n0, int lane) {
+template <bool kNK, typename SM>
+GDN2_DEV void load_b2(uint32_t* b, SM s, int k0, int n0, int lane) {
   if (kNK) {
     const int nr = n0 + (lane & 7) + (lane >> 4) * 8;
     const int kc = k0 + ((lane >> 3) & 1) * 8;
@@ -180,8 +180,10 @@ GDN2_DEV void load_b2(uint32_t* b, Smem s, int k0, int n0, int lane) {
 // Warp tile: acc[MT][NT][4] += A[m0 : m0+16*MT, 0:kdim] * B[0:kdim, n0 : n0+8*NT]
 // (NT even).  Accumulator layout per (i, j): c0,c1 at row m0+16i+g, cols
 // n0+8j+2t, +1; c2,c3 at row +8.
-template <int MT, int NT, bool kATrans, bool kBNK>
-GDN2_DEV void warp_mma(float (&acc)[MT][NT][4], Smem A, int m0, Smem B, int n0, int k_begin,
+// (SA, SB: any shared-memory view with at(r, c) -> the 16-byte row segment of
+// element (r, c), c % 8 == 0: padded rows (Smem) or swizzled tiles)
+template <int MT, int NT, bool kATrans, bool kBNK, typename SA = Smem, typename SB = Smem>
+GDN2_DEV void warp_mma(float (&acc)[MT][NT][4], SA A, int m0, SB B, int n0, int k_begin,
                        int k_end, int lane) {
   static_assert(NT % 2 == 0, "NT must be even");
 #pragma unroll 2
