@@ -384,7 +384,8 @@ def naive_torch_recurrence(q, k, v, g, b, w, scale):
 def cpu_baselines_torch():
     """BASELINE B2 (naive fp32 torch recurrence with autograd, config 1 and
     config 2 per token-head) and B4 (naive torch decode step, config 3) on
-    every host core; each sample runs for at least 5 s."""
+    every host core; each sample runs for at least 5 s and reports its median
+    call."""
     import torch
     import torch.nn.functional as F
     ncores = os.cpu_count() or 1
@@ -401,16 +402,29 @@ def cpu_baselines_torch():
         do = torch.randn(Bn, Tn, Hn, d, generator=gen)
         return [x.requires_grad_(True) for x in (q, k, v, g, b, w)], do
 
+    def median(xs):
+        xs = sorted(xs)
+        m = len(xs) // 2
+        return xs[m] if len(xs) % 2 else 0.5 * (xs[m - 1] + xs[m])
+
+    # every sample: two untimed calls (allocator and thread-pool warm-up), then
+    # calls for at least 5 s; the median call (host noise on tiny per-token ops
+    # moves the mean by >10% between runs)
     def time_fwd_bwd(Bn, Tn, Hn, d, min_s=5.0):
         leaves, do = mk(Bn, Tn, Hn, d)
-        n, tot = 0, 0.0
-        while tot < min_s:
-            t0 = time.perf_counter()
+
+        def call():
             o, _ = naive_torch_recurrence(*leaves, d ** -0.5)
             torch.autograd.grad(o, leaves, do)
-            tot += time.perf_counter() - t0
-            n += 1
-        return tot / n, n
+
+        call()
+        call()
+        ts = []
+        while sum(ts) < min_s:
+            t0 = time.perf_counter()
+            call()
+            ts.append(time.perf_counter() - t0)
+        return median(ts), len(ts)
 
     out = {"cores": ncores, "cpu": cpu_model(), "torch_threads": torch.get_num_threads()}
     t1, n1 = time_fwd_bwd(1, 256, 2, 64)
@@ -430,16 +444,21 @@ def cpu_baselines_torch():
         b = torch.sigmoid(torch.randn(DEC_N, H, K, generator=gen))
         w = torch.sigmoid(torch.randn(DEC_N, H, V, generator=gen))
         g = -F.softplus(torch.randn(DEC_N, H, K, generator=gen)) * 0.1
-        n, tot = 0, 0.0
-        while tot < 5.0:
-            t0 = time.perf_counter()
+        def step():
             S.mul_(torch.exp(g)[..., None])
             u = w * v - torch.einsum("nhkv,nhk->nhv", S, b * k)
             S.add_(k[..., None] * u[:, :, None, :])
             torch.einsum("nhkv,nhk->nhv", S, q * K ** -0.5)
-            tot += time.perf_counter() - t0
-            n += 1
-    us = 1e6 * tot / n
+
+        step()
+        step()
+        ts = []
+        while sum(ts) < 5.0:
+            t0 = time.perf_counter()
+            step()
+            ts.append(time.perf_counter() - t0)
+        n = len(ts)
+    us = 1e6 * median(ts)
     out["b4_decode"] = {"value": decode_bytes_per_step(DEC_N) / (us * 1e-6) / 1e9, "unit": "GB/s",
                         "us_per_step": us, "repeats": n,
                         "sample": "config 3 decode step: naive torch on fp32 S [256,16,128,128] in place"}
