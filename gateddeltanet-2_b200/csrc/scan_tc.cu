@@ -52,7 +52,7 @@ constexpr uint32_t kStageTx = 9 * kTileBytes + kTcK * 4;
 // two column sets by chunk parity p, so a chunk's output can still be read
 // while the next chunk's products run.
 constexpr uint32_t kColS = 0;  // S^T [128 x 128]
-// S^T Y^T [128 x 64] (one N = 128 product with the next)
+// S^T Y^T - U^T = -v_new^T [128 x 64] (forward); S^T Y^T (transition mode, U = 0)
 GDN2_DEV constexpr uint32_t col_av(int p) { return 128 + 128 * p; }
 // S^T qg^T + v_new^T Aqk^T = o^T [128 x 64]
 GDN2_DEV constexpr uint32_t col_ao(int p) { return 192 + 128 * p; }
@@ -72,6 +72,7 @@ struct alignas(1024) TcSmem {
   __nv_bfloat16 SA[2][128 * 64];  // S^T in bf16, [v][k], two 64-column blocks
   __nv_bfloat16 VN[128 * 64];     // v_new^T in bf16, [v][t]
   __nv_bfloat16 OT[2][64 * 64];   // o in bf16, [t][v], two 64-column blocks
+  __nv_bfloat16 NegI[64 * 64];    // -I [t'][t] (K-major B): the first product starts from -U^T
   uint64_t full[2], empty[2], dready[2];
   uint64_t sa_ready, sa_free, mma12, vn_ready, vst_ready, mma34, o_full, ot_free;
   uint32_t tbase;
@@ -308,6 +309,12 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const SegArg
     tc::mbar_init(&sm.ot_free, 1);
     tc::mbar_fence_init();
   }
+  for (int i = tid; i < 64 * 64; i += kTcThreads) {
+    const int r = i >> 6, c = i & 63;
+    *reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(sm.NegI) + tc::sw128_off(r, c)) =
+        __float2bfloat16_rn(r == c ? -1.f : 0.f);
+  }
+  tc::fence_proxy_async();  // -I -> the tensor core
   if (warp == kWarpMma) tc::tmem_alloc(&sm.tbase, kTmemCols);
   tc::tc_fence_before();
   __syncthreads();
@@ -383,22 +390,17 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const SegArg
       if (!(ok = warp_wait(&sm.mma12, it & 1))) break;
       tc::tc_fence_after();
       {
-        // this thread's U column (32 tokens), read while the TMEM load is in flight
+        // -v_new^T of this thread's 32 tokens (the U^T term came in with the product)
         float x[32];
         tc::tmem_ld32(tl + col_av(it & 1) + tb0, x);
         __nv_bfloat16* ucol = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(st.U[v >> 6]) +
                                                             ((v & 7) << 1));
         const int vb = (v & 63) >> 3;
         __nv_bfloat16 u[32];
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int tt = tb0 + t;
-          u[t] = uzero ? __float2bfloat16_rn(0.f) : ucol[(tt * 128 + ((vb ^ (tt & 7)) << 4)) >> 1];
-        }
         tc::tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const __nv_bfloat16 vn = __float2bfloat16_rn(tb0 + t < L ? __bfloat162float(u[t]) - x[t] : 0.f);
+          const __nv_bfloat16 vn = __float2bfloat16_rn(tb0 + t < L ? -x[t] : 0.f);
           u[t] = vn;
           x[t] = __bfloat162float(vn);
         }
@@ -431,7 +433,6 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const SegArg
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nloc > 0) {
       constexpr uint32_t kId64 = tc::idesc_bf16(128, 64, 0, 0);
-      constexpr uint32_t kId128 = tc::idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t kIdS = tc::idesc_bf16(128, 128, 0, 1);
       uint64_t* last = nullptr;  // barrier of the last commit and its phase parity
       uint32_t last_par = 0;
@@ -440,11 +441,26 @@ chunk_scan_fwd_tc_kernel(const gdn2_chunk_args a, const ChunkWs ws, const SegArg
         TcStage& st = sm.st[s];
         if (!(ok = tc::mbar_wait(&sm.full[s], (it >> 1) & 1) && tc::mbar_wait(&sm.sa_ready, it & 1))) break;
         tc::tc_fence_after();
-        // [S^T Y^T | S^T qg^T] = S^T [Y; qg]^T (without outputs S^T Y^T alone)
+        // S^T Y^T - U^T = -v_new^T: the U^T part as U^T (-I) (U as an M-major operand,
+        // 64-row blocks 8 KB apart), then S^T Y^T onto it; S^T qg^T (o's first part)
+        // into the next 64 columns (qg: rows 64-127 of each [Y; qg] block)
+        constexpr uint32_t kIdU = tc::idesc_bf16(128, 64, 1, 0);
+        if (!uzero) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc::mma_bf16(tb + col_av(it & 1), tc::sdesc_sw128(tc::smem_u32(st.U[0]) + kk * 2048, kTileBytes, 1024),
+                         kdesc(sm.NegI, kk * 32), kIdU, kk > 0);
+        }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc::mma_bf16(tb + col_av(it & 1), kdesc(sm.SA[kk >> 2], (kk & 3) * 32),
-                       kdesc(st.YQ[kk >> 2], (kk & 3) * 32), outs ? kId128 : kId64, kk > 0);
+                       kdesc(st.YQ[kk >> 2], (kk & 3) * 32), kId64, !uzero || kk > 0);
+        if (outs) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            tc::mma_bf16(tb + col_ao(it & 1), kdesc(sm.SA[kk >> 2], (kk & 3) * 32),
+                         kdesc(st.YQ[kk >> 2], 64 * 128 + (kk & 3) * 32), kId64, kk > 0);
+        }
         tc::mma_commit(&sm.mma12);
         last = &sm.mma12;
         last_par = it & 1;
