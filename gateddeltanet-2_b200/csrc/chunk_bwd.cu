@@ -290,7 +290,7 @@ struct BIntraSmemTc {
   alignas(16) float rsum[kChunk][4][2];
   alignas(16) uint8_t flag[4][K];
   alignas(16) float ptot[kBIntraThreads / K][K];
-  alignas(8) uint64_t bar[3];  // completion of the three tcgen05 product rounds
+  alignas(8) uint64_t bar[3];  // completion of the three groups of tcgen05 products
   uint32_t tbase;              // TMEM base address (512 columns)
   int nflag;
   // tiles of 64-column blocks: [block][row][64]
@@ -490,7 +490,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     __syncthreads();
     if constexpr (kTc) {
       tc::tc_fence_after();
-      // round 1 (TMEM columns: dq [0,128), dk [128,256), -dY [256,384), dAqk [384,448)):
+      // product group 1 (TMEM columns: dq [0,128), dk [128,256), -dY [256,384), dAqk [384,448)):
       //   dq = do h, dk = v_new dh, dY = dv_new h over v (h^T tiles as N-major B), dAqk = do v_new^T
       if (tid == 0) {
         constexpr uint32_t iN = tc::idesc_bf16(64, 128, 0, 1), i64 = tc::idesc_bf16(64, 64, 0, 0);
@@ -566,7 +566,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
     acc_foreach(t, m0, n0, lane, [&](float v, int r, int c) { *pDY(r, c) = __float2bfloat16_rn(-v); });
   }
   cp_wait<0>();  // A and G
-  if constexpr (kTc) tc::fence_proxy_async();  // A is a tcgen05 operand from round 2 on
+  if constexpr (kTc) tc::fence_proxy_async();  // A is a tcgen05 operand from product group 2 on
   __syncthreads();
   // the forward's exactness flags (same criterion, same G)
   for (int i = tid; i < 4 * K; i += kBIntraThreads) {
@@ -604,7 +604,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   {
     float t[1][2][4];
     if constexpr (kTc) {
-      // round 1's accumulators: dq, dk to registers, -dY to its operand tile
+      // product group 1's accumulators: dq, dk to registers, -dY to its operand tile
       b3_wait(&sm.bar[0]);
       {
         float y[1][NTk][4];
@@ -626,12 +626,12 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   }
   if constexpr (kTc) {
     tc::fence_proxy_async();  // -dY -> the tensor core
-    tc::tc_fence_before();    // round 1's columns are drained
+    tc::tc_fence_before();    // product group 1's columns are drained
   }
   __syncthreads();  // h, dh, do, v_new are dead: stage q, k, b in their place
   if constexpr (kTc) {
     tc::tc_fence_after();
-    // round 2: d(w v) = A^T dv_new -> columns [256,384), d(b k 2^G) = A^T dY -> [0,128)
+    // product group 2: d(w v) = A^T dv_new -> columns [256,384), d(b k 2^G) = A^T dY -> [0,128)
     // (A as an M-major operand, dv_new and dY as N-major ones)
     if (tid == 0) {
       constexpr uint32_t iT = tc::idesc_bf16(64, 128, 1, 1);
@@ -769,7 +769,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
   float tA[1][2][4];  // dA = dv_new (w v)^T + dY (b k 2^G)^T
   if constexpr (kTc) {
     tc::tc_fence_after();
-    // round 3: dA -> columns [384,448)
+    // product group 3: dA -> columns [384,448)
     if (tid == 0) {
       constexpr uint32_t i64 = tc::idesc_bf16(64, 64, 0, 0);
       const uint32_t tb = sm.tbase, sDVN = smem_u32(p2.DVN), sWV = smem_u32(p2.WV), sDY = smem_u32(p2.DY),
@@ -794,7 +794,7 @@ chunk_bwd_intra_kernel(gdn2_chunk_args a, gdn2_chunk_grads gr, ChunkWs ws, BwdWs
       p2.DA[r][s] = __float2bfloat16_rn((s < r && r < L) ? v : 0.f);
     });
   }
-  // d(b k 2^G) = A^T dY (tcgen05: round 2, complete since the d(w v) step)
+  // d(b k 2^G) = A^T dY (tcgen05: product group 2, complete since the d(w v) step)
   {
     float t[1][NTk][4];
     if constexpr (kTc) {
