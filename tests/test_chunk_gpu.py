@@ -363,6 +363,20 @@ def test_segmented_scan_matches_oracle(gdn2, B, T, H):
     _bwd_vs_oracle(gdn2, q, k, v, gg, b, w, h0=h0, seed=T)
 
 
+def test_segmented_scan_extreme_decay_is_exact(gdn2):
+    """The segmented scans with channels that forget almost instantly (log-decay
+    -60 per token) and a burst inside one block: the segment maps carry decays
+    that underflow to zero and the fp32 folds compose them with the surviving
+    channels; forward, final state and every gradient must still match.  B=1,
+    H=2, T=2100 runs in 11 segments."""
+    B, T, H, K, V = 1, 2100, 2, 128, 128
+    q, k, v, gg, b, w = _inputs(23, B, T, H, K, V)
+    gg[..., :8] = -60.0
+    gg[:, 1000:1004, :, 8:16] = -30.0
+    h0 = torch.randn(B, H, K, V, generator=torch.Generator().manual_seed(23)) * 0.1
+    _bwd_vs_oracle(gdn2, q, k, v, gg, b, w, h0=h0, seed=23)
+
+
 def test_segmented_scan_gate_l2norm_transposed_state(gdn2):
     """Segments with the gate and l2norm in the kernel and [V, K] states."""
     B, T, H, K, V = 1, 2300, 1, 128, 128
